@@ -1,0 +1,311 @@
+#!/usr/bin/env python3
+"""Stage 2e simulation throughput on B200 (55,000 AdEx neurons / 10,700,000
+synapses, the reference network), as one JSON line.
+
+A step is one full simulate -> inject-byte -> learn step of the network
+(AdEx + NMDA/Ca + STP + dual-trace PSW STDP + CaMKII / eligibility + delays +
+gate / modulators / inhibition), on a seeded synthetic Chinese-like UTF-8
+stream (p_CJK = 0.452, the `ref45` preset), with the phase table shifted into
+the SYNAPTOGENIC phase (plasticity gain 1) so that learning is active.
+
+  value      synaptic events / s (delivered pre-spike x synapse arrivals),
+             device-timed with CUDA events on the engine's stream, inputs
+             resident in HBM
+  e2e        the same metric through the C ABI (snn_run) with host buffers:
+             every step's input bytes copied from pinned host memory and every
+             step's spike raster + spike count copied back, wall clock
+  roofline   the synapse pass (dominant kernel): algorithmic bytes per launch
+             / its mean CUDA-event duration, against MEASURED_PEAKS.json
+
+--impl reference times the CPU oracle (the reference has no CPU path; the
+oracle is the restatement of its step) on the host cores.
+
+Multi-GPU: one process per GPU; Stage 2e at this size runs one independent
+network replica per GPU ("replicas", weak scaling), value = sum over ranks,
+time = max over ranks.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "pure-snn-language_b200"))
+
+METRIC = "synaptic events/sec (SOPS) and sim steps/sec, Stage-2e 55k/10.7M, 1–8 B200"
+UNIT = "events/s"
+PHASE_OFFSET = 5000      # SYNAPTOGENIC: plasticity gain 1
+STREAM_SEED = 42
+P_CJK = 0.452
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu):
+        self.gpu = gpu
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+                for k, n in enumerate(names):
+                    if r[5 + k].lower().startswith("active"):
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                pass
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def synapse_pass_bytes(S, S_exc, d_arr, d_disp, d_ltp, steps, first_step):
+    """Algorithmic HBM bytes of the synapse pass over `steps` steps (see
+    DESIGN.md, 'Byte model'): group id 4*S + Ca read/write 8*S_exc every
+    step; per dispatched edge 12 (alpha, beta read; value write), per arrival
+    36 (value read; plasticity record read/write), per LTP visit 32; every 10
+    steps eligibility 8*S + e1/e2 16*S + CaMKII 16*S_exc; every 1000 steps
+    alpha/beta 16*S."""
+    n10 = sum(1 for t in range(first_step, first_step + steps) if t % 10 == 0)
+    n1000 = sum(1 for t in range(first_step, first_step + steps) if t % 1000 == 0)
+    dense = steps * (4.0 * S + 8.0 * S_exc)
+    periodic = n10 * (24.0 * S + 16.0 * S_exc) + n1000 * 16.0 * S
+    events = 12.0 * d_disp + 36.0 * d_arr + 32.0 * d_ltp
+    return dense + periodic + events
+
+
+def make_net(snn, device, raster_steps=1024):
+    net = snn.Network(device=device, phase_offset=PHASE_OFFSET, raster_steps=raster_steps)
+    net.build_columns(snn.topology(n_columns=50))
+    return net
+
+
+def cpu_baseline(warmup, budget_s=12.0, threads=0):
+    """CPU oracle on a bounded sample of the same workload (all host cores)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import pyoracle as po
+    import snn_b200 as snn
+    corpus = snn.stream(1 << 20, seed=STREAM_SEED, p_cjk=P_CJK)
+    cores = threads or os.cpu_count()
+    o = po.Oracle2e(po.ref_params(50, phase_offset=PHASE_OFFSET, n_threads=cores), corpus)
+    o.run(warmup)
+    c0 = o.counters()
+    t0 = time.perf_counter()
+    n = 0
+    while n < 5 or time.perf_counter() - t0 < budget_s:
+        o.run(1)
+        n += 1
+    dt = time.perf_counter() - t0
+    c1 = o.counters()
+    o.close()
+    ev = c1.arrived - c0.arrived
+    return {"value": ev / dt, "unit": UNIT, "cores": cores, "kind": "port",
+            "steps_per_sec": n / dt,
+            "sample": f"{n} steps (after {warmup} warm-up) of the 55k/10.7M network, "
+                      f"CPU oracle, {cores} OpenMP threads"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=1000)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    warm = max(args.warmup, 3)
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import torch
+        import torch.distributed as tdist
+        import datetime
+        torch.cuda.set_device(local)
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                 device_id=torch.device("cuda", local))
+        dist = tdist
+
+    if args.impl == "reference":
+        if rank == 0:
+            cb = cpu_baseline(warm)
+            line = {"metric": METRIC, "value": cb["value"], "unit": UNIT, "n_gpus": args.gpus,
+                    "steps": args.steps, "warmup": warm,
+                    "ms_per_step": 1000.0 / cb["steps_per_sec"], "higher_is_better": True,
+                    "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                    "data": "synthetic (seeded UTF-8 stream, ref45)", "impl": "reference",
+                    "config": {"workload": "stage2e 55k neurons / 10.7M synapses, ref constants",
+                               "phase": "SYNAPTOGENIC (gain 1)"},
+                    "cpu_baseline": cb,
+                    "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
+                            "d2h_bytes_per_step": 0}}
+            print(json.dumps(line), flush=True)
+        if dist:
+            dist.destroy_process_group()
+        return
+
+    import snn_b200 as snn
+    import torch
+    torch.cuda.set_device(local)
+    corpus = snn.stream(1 << 20, seed=STREAM_SEED + rank, p_cjk=P_CJK)
+    net = make_net(snn, local)
+    net.set_corpus(corpus)
+    # warm-up (also fills the network with activity)
+    net.run(warm)
+    net.synchronize()
+    c0 = net.counters()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    net.set_profiling(True)
+    first = c0["step"]
+    with ClockSampler(local) as clk:
+        net.run(args.steps)
+        net.synchronize()
+    torch.cuda.synchronize()
+    prof = net.profile()
+    net.set_profiling(False)
+    c1 = net.counters()
+    dev_ms = prof["step_ms"]
+    arr = c1["arrivals"] - c0["arrivals"]
+    disp = c1["dispatched"] - c0["dispatched"]
+    ltp = c1["ltp_visits"] - c0["ltp_visits"]
+    # max over ranks of the device time, sum of events
+    if dist:
+        t = torch.tensor([dev_ms], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e = torch.tensor([float(arr)], device="cuda", dtype=torch.float64)
+        dist.all_reduce(e, op=dist.ReduceOp.SUM)
+        dev_ms_max, arr_all = float(t.item()), float(e.item())
+    else:
+        dev_ms_max, arr_all = dev_ms, float(arr)
+    value = arr_all / (dev_ms_max / 1000.0)
+    steps_per_sec = args.steps / (dev_ms_max / 1000.0)
+
+    # roofline of the synapse pass
+    flags = net.state("flags")
+    S = net.S
+    S_exc = int(np.count_nonzero(flags & 0x03))
+    k4 = prof["kernels"]["k_synapses"]
+    k4_bytes = synapse_pass_bytes(S, S_exc, arr, disp, ltp, args.steps, first) / args.steps
+    k4_ms = k4["ms"] / k4["launches"]
+    peak, peak_kind = measured_peaks()
+    achieved = k4_bytes / (k4_ms / 1000.0) / 1e9
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "traffic_k_synapses.json")
+    if os.path.exists(tp):
+        with open(tp) as f:
+            traffic = json.load(f).get("dram_bytes_per_launch")
+
+    # end to end through the C ABI, host buffers
+    e2e_steps = args.e2e_steps
+    n_bytes = (e2e_steps + 2) // 3
+    pin = torch.empty(n_bytes, dtype=torch.uint8, pin_memory=True)
+    pin.numpy()[:] = snn.stream(n_bytes, seed=STREAM_SEED + 1000 + rank, p_cjk=P_CJK)
+    raster = torch.empty((e2e_steps, net.words), dtype=torch.int32, pin_memory=True)
+    counts = torch.empty(e2e_steps, dtype=torch.int32, pin_memory=True)
+    ce0 = net.counters()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    rc = net.L.snn_run(net.h, e2e_steps, pin.data_ptr(), n_bytes, 1, raster.data_ptr(),
+                       counts.data_ptr())
+    net._check(rc)
+    net.synchronize()
+    wall = time.perf_counter() - t0
+    ce1 = net.counters()
+    e2e_arr = ce1["arrivals"] - ce0["arrivals"]
+    if dist:
+        t = torch.tensor([wall], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e = torch.tensor([float(e2e_arr)], device="cuda", dtype=torch.float64)
+        dist.all_reduce(e, op=dist.ReduceOp.SUM)
+        wall, e2e_arr = float(t.item()), float(e.item())
+    e2e = {"value": e2e_arr / wall, "unit": UNIT,
+           "h2d_bytes_per_step": n_bytes / e2e_steps,
+           "d2h_bytes_per_step": net.words * 4 + 4,
+           "steps_per_sec": e2e_steps / wall}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": warm, "ms_per_step": dev_ms_max / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded UTF-8 stream, ref45 preset)",
+            "steps_per_sec": steps_per_sec,
+            "config": {"workload": "stage2e 55k neurons / 10.7M synapses (reference network), "
+                                   "ref constants, SYNAPTOGENIC phase",
+                       "n_neurons": net.N, "n_synapses": S,
+                       "parallelism": "replicas" if world > 1 else "single",
+                       "l2": "inputs larger than L2 (synapse state ~0.73 GB per GPU)",
+                       "events_per_step": arr / args.steps},
+            "e2e": e2e,
+            "gpu_launches": int(sum(v["launches"] for v in prof["kernels"].values())),
+            "kernels_ms_per_step": {k: v["ms"] / max(v["launches"], 1)
+                                    for k, v in prof["kernels"].items()},
+            "roofline": {"bound": "hbm", "kernel": "k_synapses", "achieved": achieved,
+                         "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_kind": peak_kind, "bytes_per_launch": k4_bytes,
+                         "traffic": traffic},
+            "clocks": clk.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(warm)
+        print(json.dumps(line), flush=True)
+    net.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

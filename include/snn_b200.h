@@ -1,0 +1,226 @@
+/*
+ * snn_b200.h - C ABI of the B200-native spiking-network core.
+ *
+ * A thin, exception-free C boundary over the host C++ engines and their
+ * sm_100a CUDA kernels.  All device memory is owned by the context handle;
+ * host buffers are owned by the caller.  A context is used by one host
+ * thread at a time.  Every entry point returns SNN_OK (0) or an SNN_ERR_*
+ * code; snn_last_error() gives the message.  Nothing here calls exit().
+ *
+ * Each entry point replaces a piece of the reference's host C++ API
+ * (TSOFTP-afk/pure-snn-language; paths relative to that project):
+ *
+ *   snn_create / snn_destroy
+ *       stage2e::MemoryAllocator::allocate_all / free_all
+ *           (src/stage2e/memory_allocator.cuh:306-339),
+ *       SNNNetwork::SNNNetwork / ~SNNNetwork / cleanup
+ *           (src/include/network.h:11-95, src/host/network.cpp:15-26)
+ *   snn_build_columns
+ *       stage2e::init_network (src/stage2e/network_init.cuh:42,
+ *           src/stage2e/network_init.cu:573-594),
+ *       SNNNetwork::initialize / allocate_only + init_columnar_synapses
+ *           (src/host/network.cpp:78-135, src/stage2/columnar_topology.cu:47-143)
+ *   snn_set_corpus
+ *       stage2e::load_text_corpus (src/stage2e/input_encoding.cuh:35-50,
+ *           src/stage2e/input_encoding.cu:40-96)
+ *   snn_step
+ *       stage2e::BioMechanismScheduler::step(int) (src/stage2e/scheduler.cuh:75,
+ *           src/stage2e/scheduler.cu:485-676),
+ *       SNNNetwork::step(const float*, int) (src/include/network.h:29,
+ *           src/host/network.cpp:143-191)
+ *   snn_run
+ *       the per-step host loops of src/stage2e/main.cpp:679-743 and
+ *       src/stage2/unsupervised_trainer.cu:96-171, as one call
+ *   snn_set_dopamine    SNNNetwork::set_dopamine (src/include/network.h:44)
+ *   snn_set_e0          stage2e::set_e0_ablation (src/stage2e/synapse_kernels.cuh:82)
+ *                       + BioMechanismScheduler::e0_ablation (scheduler.cuh:72)
+ *   snn_get_spikes      d_spike_flags reads (src/stage2e/scheduler.cu:627-634)
+ *   snn_get_state       the raw device-pointer getters (src/include/network.h:58-67)
+ *                       and PersistentBuffers (src/stage2e/memory_allocator.cuh:226-301)
+ *   snn_get_counters    BioMechanismScheduler stats getters (scheduler.cuh:78-123),
+ *                       SNNNetwork::get_stats (src/include/network.h:40)
+ *   snn_save / snn_load SNNNetwork::save_weights / load_weights
+ *                       (src/host/network.cpp:224-290), save_checkpoint /
+ *                       load_checkpoint (src/stage2/unsupervised_trainer.cu:176-348),
+ *                       BioMechanismScheduler::save_checkpoint (scheduler.cu:402-483)
+ */
+#ifndef SNN_B200_H
+#define SNN_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------- */
+#define SNN_OK 0
+#define SNN_ERR_ARG 1          /* bad argument / size mismatch            */
+#define SNN_ERR_CUDA 2         /* CUDA runtime error (message has detail) */
+#define SNN_ERR_OOM 3          /* device or host allocation failed        */
+#define SNN_ERR_STATE 4        /* call out of order (e.g. step before build) */
+#define SNN_ERR_IO 5           /* file missing / truncated / bad magic    */
+#define SNN_ERR_UNSUPPORTED 6  /* option not available for this model    */
+#define SNN_ERR_NO_DEVICE 7    /* no CUDA device visible                  */
+
+/* ---- models and presets ---------------------------------------------- */
+#define SNN_MODEL_STAGE2E 0  /* AdEx + NMDA/Ca + STP + PSW STDP + delays   */
+#define SNN_MODEL_STAGE0 1   /* LIF + pair STDP + eligibility + dopamine   */
+
+#define SNN_PRESET_REF 0      /* constants exactly as the reference kernels */
+#define SNN_PRESET_BASELINE 1 /* constants as stated in the benchmark spec  */
+
+typedef struct snn_ctx snn_ctx;
+
+typedef struct snn_config {
+    int32_t model;         /* SNN_MODEL_*                                     */
+    int32_t preset;        /* SNN_PRESET_*                                    */
+    int32_t device;        /* CUDA device ordinal                             */
+    int32_t e0;            /* Stage 2e E0 ablation (pure STDP)                 */
+    int32_t phase_offset;  /* Stage 2e: added to the step for the phase table */
+    int32_t raster_steps;  /* device spike-raster capacity in steps (0 = 1024) */
+    int32_t reserved[10];
+} snn_config;
+
+/* Network construction by columns and layers.
+ * Stage 2e: n_columns cortical columns of l4/l23/l5/l6 neurons plus
+ *   pf_groups prefrontal groups of pf_group_size neurons, generated with the
+ *   reference rules (src/stage2e/network_init.cu:158-473) when rule == 0.
+ * Stage 0: n_columns == 0 gives the single-block 2000/6000/2000 network; with
+ *   n_columns > 0 each column is l4 (sensory) / l23 (association) / l5
+ *   (motor) neurons. */
+typedef struct snn_topology_spec {
+    int32_t n_columns;
+    int32_t l4, l23, l5, l6;
+    int32_t pf_groups, pf_group_size;
+    int32_t deg_intra, deg_inter, deg_l5_pf, deg_pf_self, deg_pf_assoc;
+    int64_t total_synapses;
+    uint32_t seed;
+    int32_t rule;          /* 0 = reference generator; 1 = uniform out-degree */
+    int32_t reserved[8];
+} snn_topology_spec;
+
+typedef struct snn_counters {
+    int64_t step;            /* steps executed                              */
+    int64_t total_spikes;
+    int64_t arrivals;        /* delivered (pre-spike, synapse) events       */
+    int64_t dispatched;      /* out-edges of spiking neurons                */
+    int64_t dropped_ref;     /* events the reference's 750K slots would drop */
+    int64_t ltp_visits;      /* incoming synapses of spiking neurons        */
+    int64_t burst_spikes;    /* spikes within 5 steps of the previous one   */
+    int64_t n_neurons;
+    int64_t n_synapses;
+    int64_t n_groups;        /* Stage 2e (pre, delay, class) synapse groups */
+    int32_t last_spikes;     /* spikes of the last executed step            */
+    int32_t last_byte;       /* byte injected at the last step, -1 = none   */
+    double modeled_bytes;    /* algorithmic HBM bytes of the executed steps */
+    int64_t reserved[6];
+} snn_counters;
+
+/* fields for snn_get_state (host_buf gets n elements of the listed type;
+ * synapse fields are returned in the reference's pre-major synapse order) */
+enum {
+    SNN_STATE_V = 0,           /* f32[N] membrane potential                 */
+    SNN_STATE_W_ADAPT = 1,     /* f32[N] AdEx adaptation w                  */
+    SNN_STATE_SYN_CURRENT = 2, /* f32[N] leaky synaptic current s           */
+    SNN_STATE_FIRE_RATE = 3,   /* f32[N]                                    */
+    SNN_STATE_CA_NEURON = 4,   /* f32[N]                                    */
+    SNN_STATE_INPUT = 5,       /* f32[N] input current for the next step    */
+    SNN_STATE_NMDA_CUR = 6,    /* f32[N] NMDA current for the next step     */
+    SNN_STATE_LAST_SPIKE = 7,  /* i32[N]                                    */
+    SNN_STATE_REFRACTORY = 8,  /* i32[N]                                    */
+    SNN_STATE_X_POST = 9,      /* f32[N] post trace                         */
+    SNN_STATE_THRESH_OFF = 10, /* i32[N] threshold offset (fixed point)     */
+    SNN_STATE_ALPHA = 20,      /* f32[S] PSW alpha                          */
+    SNN_STATE_BETA = 21,       /* f32[S] PSW beta                           */
+    SNN_STATE_WEIGHT = 22,     /* f32[S] weight (derived for Stage 2e)      */
+    SNN_STATE_X_PRE = 23,      /* f32[S]                                    */
+    SNN_STATE_NMDA_G = 24,     /* f32[S]                                    */
+    SNN_STATE_CA = 25,         /* f32[S]                                    */
+    SNN_STATE_RESOURCE = 26,   /* f32[S] STP R                              */
+    SNN_STATE_UTIL = 27,       /* f32[S] STP u                              */
+    SNN_STATE_ELIG = 28,       /* f32[S]                                    */
+    SNN_STATE_CAMKII_ACT = 29, /* f32[S]                                    */
+    SNN_STATE_CAMKII_AUTO = 30,/* f32[S]                                    */
+    SNN_STATE_E1 = 31,         /* f32[S]                                    */
+    SNN_STATE_E2 = 32,         /* f32[S]                                    */
+    SNN_STATE_POST = 40,       /* i32[S] post neuron of each synapse        */
+    SNN_STATE_DELAY = 41,      /* u8[S]                                     */
+    SNN_STATE_ROW_PTR = 42,    /* i32[N+1] pre-major CSR row pointer        */
+    SNN_STATE_FLAGS = 43,      /* u8[S] receptor flags                      */
+    SNN_STATE_GATES = 50,      /* f32[4*n_columns] gate, act_ema, nov_ema, l6_ema */
+    SNN_STATE_MODULATORS = 51, /* f32[4] DA, ACh, NE, 5HT                   */
+    SNN_STATE_BYTE_HIST = 52,  /* i32[256] spikes per injected byte         */
+    SNN_STATE_NEURON_BYTE_COUNTS = 53 /* i32[N*256]                         */
+};
+
+/* on-disk formats for snn_save / snn_load */
+enum {
+    SNN_FMT_NATIVE = 0,   /* full state, bit-exact resume                  */
+    SNN_FMT_SNN2_V1 = 1,  /* src/stage2/unsupervised_trainer.cu:176-262     */
+    SNN_FMT_SCKP_V2 = 2,  /* src/stage2e/scheduler.cu:411-483 (save only in the reference) */
+    SNN_FMT_RAW_F32 = 3   /* src/host/network.cpp:224-290                   */
+};
+
+int snn_config_init(snn_config* cfg, int32_t model, int32_t preset);
+int snn_topology_init(snn_topology_spec* spec, int32_t model, int32_t n_columns);
+int snn_create(const snn_config* cfg, snn_ctx** out);
+void snn_destroy(snn_ctx* ctx);
+const char* snn_last_error(const snn_ctx* ctx);
+const char* snn_version(void);
+
+int snn_build_columns(snn_ctx* ctx, const snn_topology_spec* spec);
+
+/* Text stream with the reference semantics: one byte per inject step,
+ * wrapping at the end (src/stage2e/input_encoding.cu:192-203).  The bytes
+ * are copied to device memory. */
+int snn_set_corpus(snn_ctx* ctx, const uint8_t* bytes, int64_t n);
+
+/* One step.  `step` must equal the number of steps executed so far.
+ * Stage 2e: on steps with step % 3 == 0 the byte is inject_byte if >= 0,
+ *   else the next corpus byte (or (step/3)%256 without a corpus).
+ * Stage 0: inject_byte >= 0 drives its one-hot input, -1 = no input.
+ * learn = 0 freezes plasticity (gain forced to 0). */
+int snn_step(snn_ctx* ctx, int32_t step, int32_t inject_byte, int32_t learn);
+
+/* n_steps steps as one call, with no host synchronisation between steps.
+ * bytes (nullable) replaces the corpus for this and later calls.  If
+ * raster_out is non-null it receives n_steps spike bitmasks of
+ * ceil(N/32) words each; counts_out (nullable) receives n_steps spike counts. */
+int snn_run(snn_ctx* ctx, int32_t n_steps, const uint8_t* bytes, int64_t n_bytes,
+            int32_t learn, uint32_t* raster_out, int32_t* counts_out);
+
+int snn_synchronize(snn_ctx* ctx);
+int snn_get_spikes(snn_ctx* ctx, uint32_t* bitmask, int64_t n_words);
+int snn_get_state(snn_ctx* ctx, int32_t which, void* host_buf, int64_t n_bytes);
+int snn_get_counters(snn_ctx* ctx, snn_counters* out);
+int snn_set_dopamine(snn_ctx* ctx, float level);
+int snn_set_e0(snn_ctx* ctx, int32_t enable);
+/* Device timing of the engine's kernels: CUDA events recorded on the engine
+ * stream around every kernel of every step (captured into the step graph).
+ * Cumulative since snn_set_profiling(ctx, 1). */
+typedef struct snn_profile {
+    int64_t steps;           /* steps timed                                  */
+    int32_t n_kernels;       /* kernels per step                              */
+    int32_t reserved0;
+    double kernel_ms[8];     /* summed device time per kernel slot            */
+    int64_t launches[8];     /* launches per kernel slot                      */
+    double step_ms;          /* summed device time of whole steps             */
+    char names[8][32];       /* kernel names                                  */
+} snn_profile;
+int snn_set_profiling(snn_ctx* ctx, int32_t enable);
+int snn_get_profile(snn_ctx* ctx, snn_profile* out);
+
+int snn_save(snn_ctx* ctx, const char* path, int32_t fmt);
+int snn_load(snn_ctx* ctx, const char* path, int32_t fmt);
+
+/* Seeded synthetic UTF-8 byte stream: a fraction p_cjk of characters are
+ * CJK code points U+4E00..U+9FFF drawn Zipf(zipf_s) by rank (rank -> code
+ * point through a seeded permutation), 3 bytes each; the rest are ASCII
+ * space (90 %) or one of ",.!?;:".  Writes exactly n bytes. */
+int snn_stream_generate(uint8_t* out, int64_t n, uint64_t seed, double p_cjk, double zipf_s);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SNN_B200_H */

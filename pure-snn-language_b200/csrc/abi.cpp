@@ -1,0 +1,205 @@
+// abi.cpp - extern "C" boundary: handle management, error codes, dispatch to
+// the engines.  No exception crosses this boundary and nothing calls exit().
+#include <cstdio>
+#include <memory>
+#include <string>
+#include "common.h"
+
+struct snn_ctx {
+    snn_config cfg;
+    std::unique_ptr<snnb::Engine> eng;
+    std::string err;
+};
+
+namespace {
+thread_local std::string g_create_err;
+
+template <typename F>
+int guard(snn_ctx* ctx, F&& f) {
+    if (!ctx) return SNN_ERR_ARG;
+    try {
+        f();
+        ctx->err.clear();
+        return SNN_OK;
+    } catch (const snnb::Error& e) {
+        ctx->err = e.what();
+        return e.code;
+    } catch (const std::bad_alloc&) {
+        ctx->err = "host allocation failed";
+        return SNN_ERR_OOM;
+    } catch (const std::exception& e) {
+        ctx->err = e.what();
+        return SNN_ERR_STATE;
+    }
+}
+
+snn_topology_spec reference_columns(int32_t n_columns) {
+    snn_topology_spec s;
+    memset(&s, 0, sizeof(s));
+    s.n_columns = n_columns;
+    s.l4 = 200; s.l23 = 350; s.l5 = 200; s.l6 = 250;
+    s.pf_groups = n_columns; s.pf_group_size = 100;
+    s.deg_intra = 150; s.deg_inter = 30; s.deg_l5_pf = 15;
+    s.deg_pf_self = 100; s.deg_pf_assoc = 50;
+    s.total_synapses = (int64_t)10700000 * n_columns / 50;
+    s.seed = 42;
+    s.rule = 0;
+    return s;
+}
+}  // namespace
+
+extern "C" {
+
+const char* snn_version(void) { return "snn_b200 0.1 (sm_100a)"; }
+
+int snn_config_init(snn_config* cfg, int32_t model, int32_t preset) {
+    if (!cfg) return SNN_ERR_ARG;
+    if (model != SNN_MODEL_STAGE2E && model != SNN_MODEL_STAGE0) return SNN_ERR_ARG;
+    if (preset != SNN_PRESET_REF && preset != SNN_PRESET_BASELINE) return SNN_ERR_ARG;
+    memset(cfg, 0, sizeof(*cfg));
+    cfg->model = model;
+    cfg->preset = preset;
+    cfg->raster_steps = 1024;
+    return SNN_OK;
+}
+
+int snn_topology_init(snn_topology_spec* spec, int32_t model, int32_t n_columns) {
+    if (!spec) return SNN_ERR_ARG;
+    if (model == SNN_MODEL_STAGE2E) {
+        if (n_columns < 2) return SNN_ERR_ARG;
+        *spec = reference_columns(n_columns);
+        return SNN_OK;
+    }
+    if (model == SNN_MODEL_STAGE0) {
+        memset(spec, 0, sizeof(*spec));
+        spec->n_columns = n_columns;  // 0 = Stage 0 single block
+        if (n_columns == 0) { spec->l4 = 2000; spec->l23 = 6000; spec->l5 = 2000; }
+        else { spec->l4 = 200; spec->l23 = 600; spec->l5 = 200; }
+        spec->deg_intra = 100;
+        spec->seed = 42;
+        spec->rule = 1;
+        return SNN_OK;
+    }
+    return SNN_ERR_ARG;
+}
+
+int snn_create(const snn_config* cfg, snn_ctx** out) {
+    if (!cfg || !out) return SNN_ERR_ARG;
+    *out = nullptr;
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+        cudaGetLastError();
+        return SNN_ERR_NO_DEVICE;
+    }
+    if (cfg->device < 0 || cfg->device >= ndev) return SNN_ERR_ARG;
+    snn_ctx* ctx = new (std::nothrow) snn_ctx();
+    if (!ctx) return SNN_ERR_OOM;
+    ctx->cfg = *cfg;
+    int rc = guard(ctx, [&] {
+        if (cfg->model == SNN_MODEL_STAGE2E) ctx->eng.reset(snnb::make_engine_stage2e(*cfg));
+        else if (cfg->model == SNN_MODEL_STAGE0) ctx->eng.reset(snnb::make_engine_stage0(*cfg));
+        else throw snnb::Error(SNN_ERR_ARG, "unknown model");
+    });
+    if (rc != SNN_OK) {
+        g_create_err = ctx->err;
+        delete ctx;
+        return rc;
+    }
+    *out = ctx;
+    return SNN_OK;
+}
+
+void snn_destroy(snn_ctx* ctx) { delete ctx; }
+
+const char* snn_last_error(const snn_ctx* ctx) {
+    return ctx ? ctx->err.c_str() : g_create_err.c_str();
+}
+
+int snn_build_columns(snn_ctx* ctx, const snn_topology_spec* spec) {
+    return guard(ctx, [&] {
+        SNN_REQUIRE(spec, SNN_ERR_ARG, "null topology");
+        ctx->eng->build(*spec);
+    });
+}
+
+int snn_set_corpus(snn_ctx* ctx, const uint8_t* bytes, int64_t n) {
+    return guard(ctx, [&] { ctx->eng->set_corpus(bytes, n); });
+}
+
+int snn_step(snn_ctx* ctx, int32_t step, int32_t inject_byte, int32_t learn) {
+    return guard(ctx, [&] {
+        SNN_REQUIRE(step == ctx->eng->steps_done(), SNN_ERR_STATE,
+                    "step index must equal the number of executed steps");
+        SNN_REQUIRE(inject_byte >= -1 && inject_byte < 256, SNN_ERR_ARG, "inject_byte out of range");
+        ctx->eng->run(1, inject_byte, learn, nullptr, nullptr);
+    });
+}
+
+int snn_run(snn_ctx* ctx, int32_t n_steps, const uint8_t* bytes, int64_t n_bytes, int32_t learn,
+            uint32_t* raster_out, int32_t* counts_out) {
+    return guard(ctx, [&] {
+        SNN_REQUIRE(n_steps >= 0, SNN_ERR_ARG, "negative step count");
+        if (bytes) ctx->eng->set_corpus(bytes, n_bytes);
+        ctx->eng->run(n_steps, -1, learn, raster_out, counts_out);
+    });
+}
+
+int snn_synchronize(snn_ctx* ctx) {
+    return guard(ctx, [&] { ctx->eng->sync(); });
+}
+
+int snn_get_spikes(snn_ctx* ctx, uint32_t* bitmask, int64_t n_words) {
+    return guard(ctx, [&] {
+        SNN_REQUIRE(bitmask, SNN_ERR_ARG, "null buffer");
+        ctx->eng->get_spikes(bitmask, n_words);
+    });
+}
+
+int snn_get_state(snn_ctx* ctx, int32_t which, void* host_buf, int64_t n_bytes) {
+    return guard(ctx, [&] {
+        SNN_REQUIRE(host_buf, SNN_ERR_ARG, "null buffer");
+        ctx->eng->get_state(which, host_buf, n_bytes);
+    });
+}
+
+int snn_get_counters(snn_ctx* ctx, snn_counters* out) {
+    return guard(ctx, [&] {
+        SNN_REQUIRE(out, SNN_ERR_ARG, "null counters");
+        ctx->eng->counters(out);
+    });
+}
+
+int snn_set_dopamine(snn_ctx* ctx, float level) {
+    return guard(ctx, [&] { ctx->eng->set_dopamine(level); });
+}
+
+int snn_set_e0(snn_ctx* ctx, int32_t enable) {
+    return guard(ctx, [&] { ctx->eng->set_e0(enable); });
+}
+
+int snn_set_profiling(snn_ctx* ctx, int32_t enable) {
+    return guard(ctx, [&] { ctx->eng->set_profiling(enable); });
+}
+
+int snn_get_profile(snn_ctx* ctx, snn_profile* out) {
+    return guard(ctx, [&] {
+        SNN_REQUIRE(out, SNN_ERR_ARG, "null profile");
+        ctx->eng->get_profile(out);
+    });
+}
+
+int snn_save(snn_ctx* ctx, const char* path, int32_t fmt) {
+    return guard(ctx, [&] {
+        SNN_REQUIRE(path, SNN_ERR_ARG, "null path");
+        ctx->eng->save(path, fmt);
+    });
+}
+
+int snn_load(snn_ctx* ctx, const char* path, int32_t fmt) {
+    return guard(ctx, [&] {
+        SNN_REQUIRE(path, SNN_ERR_ARG, "null path");
+        ctx->eng->load(path, fmt);
+    });
+}
+
+}  // extern "C"

@@ -1,0 +1,1142 @@
+// engine2e.cu - Stage 2e engine on sm_100a: AdEx neurons, NMDA/Ca synapses,
+// Tsodyks-Markram STP, dual-trace PSW STDP, CaMKII / eligibility, axonal
+// delays, thalamic gate, modulators and inhibition, one step = 3 kernels:
+//
+//   k_control   (1 CTA)     deferred control of step t-1 (inhibition drive,
+//                           modulators / TD value function, statistics),
+//                           thalamic gate, byte, phase gain, M_ij of step t
+//   k_neurons   (N threads) population-coded input, inhibition, AdEx update,
+//                           spike history / raster / counters, Mg block and
+//                           post trace of the neuron, then the update of the
+//                           neuron's outgoing synapse groups (NMDA g, pre
+//                           trace, STP) and their per-step view
+//   k_synapses  (warp/post) post-major pass over every neuron's incoming
+//                           synapses: Ca / NMDA current, LTP (post spike),
+//                           LTD (arrival), dispatch value capture, input
+//                           current for the next step, CaMKII / eligibility
+//                           fold every 10 steps, PSW decay every 1000 steps
+//
+// Semantics follow src/stage2e/scheduler.cu:485-676 step for step; the CPU
+// oracle (oracle/oracle2e.cpp) states the same semantics with per-synapse
+// state, so bit equality with it also checks the exact invariants used here:
+//   - x_post and last_post depend only on the post neuron (one per neuron);
+//   - R, u, NMDA g and x_pre depend only on (pre, effective delay, FF flag):
+//     one "group" per such triple, updated once per step by the pre's thread;
+//   - the weight is 1.5*alpha/(alpha+beta) with the pre's sign, derived when
+//     needed instead of stored; inhibitory synapses keep Ca, NMDA g and
+//     CaMKII at exactly 0 and are skipped by those updates;
+//   - modulator concentrations are identical for every neuron, so M_ij takes
+//     one of two values (excitatory / inhibitory pre) per step.
+// Delivery is pulled: synapse s of neuron j receives at step T iff its pre
+// spiked at T - d_s (32-step spike history per neuron).  The value delivered
+// is w*R captured at dispatch; synapses with d >= 2 keep it in an 8-slot
+// ring indexed by floor(t_dispatch / 3) mod 8 (the 2-step refractory period
+// makes dispatches of one synapse >= 3 steps apart, and d <= 19 keeps at most
+// 7 in flight, so slots never collide).
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <memory>
+#include "common.h"
+#include "net2e.h"
+#include "snn_pmath.h"
+
+namespace snn2e {
+
+constexpr int NCLASS = 3;  // STP classes: 0 feed-forward, 1 excitatory, 2 inhibitory
+constexpr int VAL_SLOTS = 8;
+constexpr int TD_DIM = 200;
+
+// group view flag bits (view.w holds them as raw bits)
+constexpr uint32_t GV_D_MASK = 0x1f, GV_FF = 1u << 5, GV_EXC = 1u << 6, GV_ARR = 1u << 7,
+                   GV_NEXT = 1u << 8, GV_DISP = 1u << 9;
+
+struct Consts {
+    // neuron (normalised AdEx, src/stage2e/neuron_kernels.cu:85-165)
+    float syn_keep, syn_in, vt, dT, inv_taum, a_ad, inv_tauw, b_ad, vmin, vmax;
+    float ca_n_inc, ca_n_dec, fr_refr, fr_spk_keep, fr_spk_add, fr_quiet, off_decay;
+    int refr_steps, off_add, off_max;
+    // synapse
+    float dec_nmda, dec_ca, dec_ca_ff, ca_max, ca_max_ff, rec_ff_step, dec_xpre, dec_xpost;
+    float g_nmda, ca_gain, e_rev, i_gain, i_min;
+    float U[NCLASS], fac[NCLASS], rec[NCLASS];
+    float a_plus, a_minus, w_max, eta, eta_ff, reb_thr, reb_gain, ab_min, ab_reset, psw_decay;
+    float e1_dec, e2_dec;
+    float ck_k1, ck_k2, ck_k3, ck_k4, ck_pp1, ck_dt;
+    // modulators
+    float mod_dec[4], rec_da[2], rec_ach, rec_ne, rec_ht5;
+    // input
+    float pop_gain, gain_in, gain_out;
+    int pop_k, pref_range, inject_interval;
+};
+
+struct Ctrl {
+    long long next_t, t;
+    int inject, byte;
+    float gain, prune_thr, M[2];
+    float gdrive;
+    int kwta_k, inh_active;
+    int learn, byte_override, e0, phase_offset;
+    long long total_steps, total_spikes, inject_spikes;
+    int last_spikes;
+    float conc[4];
+    long long corpus_len, corpus_pos;
+    unsigned long long arrivals, dispatched, ltp_visits, burst, dropped_ref;
+    int step_spikes[2];
+    unsigned long long step_arrivals[2];
+    long long raster_base;  // step whose raster is in row 0
+};
+
+struct Dev {
+    // neurons
+    float *V, *wad, *s, *fr, *can, *xpost, *mg, *input, *nmda_cur;
+    int *last, *ref;
+    unsigned short* off;
+    unsigned* info;  // type | region<<1 | subtype<<4 | column<<8 (0xffffff = PF)
+    unsigned* hist;
+    int *gbeg, *in_ptr;
+    // groups
+    unsigned* gmeta;
+    int* gsize;
+    float4* gstate;  // R, u, nmda, xpre
+    float4* gview;   // nmda, xpre_ltp, R_dispatch, flags
+    // synapses (post-major)
+    unsigned* gid;
+    float* ca;
+    float4* ev;      // alpha, beta, autophosphorylation, eligibility
+    float *act, *e1, *e2;
+    float* val;      // VAL_SLOTS per synapse
+    // control
+    Ctrl* ctrl;
+    float4* gates;   // gate, act_ema, nov_ema, l6_ema
+    int *col_sp, *l6_sp, *sub_sp;  // [2][ncol], [2][ncol], [2][TD_DIM]
+    unsigned* byte_hist_nov;
+    int* byte_histogram;
+    int* neuron_byte_counts;
+    float *w_value, *w_pred, *baseline;
+    const unsigned char* corpus;
+    unsigned* raster;
+    int raster_cap, words;
+    int N, N_assoc, NPC, ncol, l4, per_sub;
+};
+
+__device__ __forceinline__ int phase_of(long long step) {
+    return step < 5000 ? 0 : step < 200000 ? 1 : step < 800000 ? 2 : step < 1500000 ? 3 : 4;
+}
+__constant__ float c_phase_gain[5] = {0.0f, 1.0f, 3.0f, 1.0f, 0.3f};
+__constant__ float c_phase_prune[5] = {0.0f, 0.0f, 0.0f, 0.05f, 0.02f};
+
+__device__ __forceinline__ float clampf(float x, float lo, float hi) {
+    if (x < lo) x = lo;
+    if (x > hi) x = hi;
+    return x;
+}
+
+// ---------------------------------------------------------------------------
+// k_control: one CTA.  src/stage2e/scheduler.cu:485-540 (gate, byte) and the
+// deferred end-of-step host work of step t-1 (:569-670, :688-751).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) k_control(Dev d, Consts k) {
+    Ctrl* c = d.ctrl;
+    __shared__ long long s_t;
+    __shared__ int s_inject, s_byte, s_prev_ok;
+    __shared__ unsigned s_total_h, s_bc;
+    const int tid = threadIdx.x;
+    if (tid == 0) {
+        long long t = c->next_t;
+        c->t = t;
+        c->next_t = t + 1;
+        s_t = t;
+        const long long prev = t - 1;
+        s_prev_ok = prev >= 0;
+        c->inh_active = 0;
+        if (prev >= 0) {
+            const int sp_prev = c->step_spikes[prev & 1];
+            const float avg = c->total_steps > 0
+                                  ? pm_div(pm_ll2f(c->total_spikes), pm_ll2f(c->total_steps))
+                                  : 0.0f;
+            // inhibition of step prev (scheduler.cu:688-722), applied at step t
+            if (prev % 10 == 0) {
+                float drive = pm_div(pm_i2f(c->last_spikes), pm_add(avg, 1.0f));
+                drive = clampf(drive, 0.0f, 2.0f);
+                c->gdrive = pm_mul(drive, 0.15f);
+                int kk = (int)pm_mul(pm_div(avg, pm_i2f(d.ncol)), 0.5f);
+                c->kwta_k = kk < 3 ? 3 : (kk > 5 ? 5 : kk);
+                c->inh_active = 1;
+            }
+            // modulators of step prev (scheduler.cu:724-751, modulatory_kernels.cu:176-254)
+            if (prev % 100 == 0 && !c->e0) {
+                float cur = pm_i2f(c->last_spikes);
+                float nov = avg > 0.0f ? pm_div(fabsf(pm_sub(cur, avg)), pm_add(avg, 1.0f)) : 0.0f;
+                if (nov > 1.0f) nov = 1.0f;
+                float pred = (cur > 10.0f && cur < 1000.0f) ? 0.5f : 0.1f;
+                float reward = pm_add(pm_mul(0.5f, nov), pm_mul(0.3f, pred));
+                const int* sub = d.sub_sp + (prev & 1) * TD_DIM;
+                const float per = pm_i2f(d.per_sub);
+                float vs = 0.0f;
+                for (int q = 0; q < TD_DIM; ++q)
+                    vs = pm_fma(d.w_value[q], pm_div(pm_i2f(sub[q]), per), vs);
+                const float om = pm_sub(1.0f, 0.99f);
+                float vsp = 0.0f;
+                for (int q = 0; q < TD_DIM; ++q) {
+                    float f = pm_div(pm_i2f(sub[q]), per);
+                    float b = pm_fma(0.99f, d.baseline[q], pm_mul(om, f));
+                    d.baseline[q] = b;
+                    vsp = pm_fma(d.w_value[q], pm_mul(d.w_pred[q], f), vsp);
+                }
+                float delta = pm_sub(pm_add(reward, pm_mul(0.9f, vsp)), vs);
+                for (int q = 0; q < TD_DIM; ++q) {
+                    float f = pm_div(pm_i2f(sub[q]), per);
+                    d.w_value[q] = clampf(pm_fma(pm_mul(0.001f, delta), f, d.w_value[q]), -1.0f, 1.0f);
+                    float pe = pm_sub(f, d.baseline[q]);
+                    d.w_pred[q] = pm_fma(pm_mul(0.001f, pe), f, d.w_pred[q]);
+                }
+                float sig[4];
+                sig[0] = pm_add(0.1f, delta > 0.0f ? delta : pm_mul(0.3f, delta));
+                if (sig[0] < 0.0f) sig[0] = 0.0f;
+                sig[1] = pm_add(pm_add(0.2f, pm_mul(0.3f, nov)), pm_mul(0.1f, pred));
+                sig[2] = 0.05f;
+                sig[3] = 0.1f;
+                if (delta < -0.5f) sig[3] = pm_add(sig[3], pm_mul(0.3f, fabsf(delta)));
+                for (int m = 0; m < 4; ++m)
+                    c->conc[m] = clampf(pm_fma(c->conc[m], k.mod_dec[m], sig[m]), 0.0f, 2.0f);
+            }
+            // statistics of step prev (scheduler.cu:627-670)
+            c->total_steps += 1;
+            c->total_spikes += sp_prev;
+            if (prev % k.inject_interval == 0) c->inject_spikes += sp_prev;
+            c->last_spikes = sp_prev;
+            unsigned long long arr = c->step_arrivals[prev & 1];
+            if (arr > 750000ull) c->dropped_ref += arr - 750000ull;
+        }
+        // phase, byte, M_ij of step t
+        const int ph = phase_of(t + c->phase_offset);
+        c->gain = c->learn ? c_phase_gain[ph] : 0.0f;
+        c->prune_thr = c_phase_prune[ph];
+        const int inj = (t % k.inject_interval) == 0;
+        int byte = 0;
+        if (inj) {
+            if (c->byte_override >= 0) {
+                byte = c->byte_override;
+            } else if (c->corpus_len > 0) {
+                byte = d.corpus[c->corpus_pos];
+                c->corpus_pos = (c->corpus_pos + 1) % c->corpus_len;
+            } else {
+                byte = (int)((t / k.inject_interval) % 256);
+            }
+        }
+        c->byte_override = -1;
+        c->inject = inj;
+        c->byte = inj ? byte : -1;
+        s_inject = inj;
+        s_byte = byte;
+        for (int e = 0; e < 2; ++e) {
+            if (c->e0) { c->M[e] = 1.0f; continue; }
+            float z = pm_mul(k.rec_da[e], c->conc[0]);
+            z = pm_fma(k.rec_ach, c->conc[1], z);
+            z = pm_fma(k.rec_ne, c->conc[2], z);
+            z = pm_fma(k.rec_ht5, c->conc[3], z);
+            c->M[e] = pm_div(1.0f, pm_add(1.0f, snn_expf(-z)));
+        }
+        unsigned tot = 0;
+        for (int b = 0; b < 256; ++b) tot += d.byte_hist_nov[b];
+        s_total_h = tot;
+        s_bc = d.byte_hist_nov[byte];
+        // fresh per-step counters for step t
+        c->step_spikes[t & 1] = 0;
+        c->step_arrivals[t & 1] = 0ull;
+    }
+    __syncthreads();
+    const long long t = s_t;
+    // zero this step's column / sub-column counters
+    for (int q = tid; q < d.ncol; q += blockDim.x) {
+        d.col_sp[(t & 1) * d.ncol + q] = 0;
+        d.l6_sp[(t & 1) * d.ncol + q] = 0;
+    }
+    for (int q = tid; q < TD_DIM; q += blockDim.x) d.sub_sp[(t & 1) * TD_DIM + q] = 0;
+    // thalamic gate of step t from the counts of step t-1 (thalamic_gate.cu:53-142)
+    for (int col = tid; col < d.ncol; col += blockDim.x) {
+        float4 g = d.gates[col];
+        float cur = s_prev_ok ? pm_i2f(d.col_sp[((t - 1) & 1) * d.ncol + col]) : 0.0f;
+        float l6c = s_prev_ok ? pm_i2f(d.l6_sp[((t - 1) & 1) * d.ncol + col]) : 0.0f;
+        float den = g.y > 1.0f ? g.y : 1.0f;
+        float an = fminf(1.0f, fmaxf(-1.0f, pm_div(pm_sub(g.y, cur), den)));
+        float l6d = g.w > 1.0f ? g.w : 1.0f;
+        float l6n = fminf(1.0f, fmaxf(-1.0f, pm_div(pm_sub(g.w, l6c), l6d)));
+        float nov = 0.0f;
+        if (s_inject) {
+            unsigned tm = s_total_h > 1u ? s_total_h : 1u;
+            nov = pm_sub(1.0f, pm_div(pm_u2f(s_bc), pm_u2f(tm)));
+            nov = fminf(1.0f, fmaxf(0.0f, nov));
+        }
+        const float om99 = pm_sub(1.0f, 0.99f), om95 = pm_sub(1.0f, 0.95f);
+        g.y = pm_fma(0.99f, g.y, pm_mul(om99, cur));
+        g.w = pm_fma(0.99f, g.w, pm_mul(om99, l6c));
+        g.z = pm_fma(0.95f, g.z, pm_mul(om95, nov));
+        float tg = pm_fma(0.3f, an, 0.5f);
+        tg = pm_fma(0.2f, g.z, tg);
+        tg = pm_fma(0.15f, l6n, tg);
+        tg = fminf(0.9f, fmaxf(0.1f, tg));
+        g.x = pm_fma(0.01f, pm_sub(tg, g.x), g.x);
+        g.x = fminf(1.0f, fmaxf(0.0f, g.x));
+        d.gates[col] = g;
+    }
+    __syncthreads();
+    if (tid == 0 && s_inject) d.byte_hist_nov[s_byte] += (unsigned)d.ncol;
+}
+
+// ---------------------------------------------------------------------------
+// k_neurons: one thread per neuron.
+//   input .......... input_encoding.cu:117-164 (hashes recomputed per L4 neuron,
+//                    duplicates added in hash order)
+//   inhibition ..... scheduler.cu:112-133 + 234-265 (computed at step t from
+//                    fire rates / column counts of step t-1, as the reference
+//                    writes it after step t-1 for the step-t update)
+//   AdEx ........... neuron_kernels.cu:61-165
+//   groups ......... synapse_kernels.cu:123-141 (arrival conductance), :84-94
+//                    (decays, FF recovery), :176-194 / :282 (pre trace),
+//                    :334-387 (STP)
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) k_neurons(Dev d, Consts k) {
+    const Ctrl* c = d.ctrl;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    const long long t = c->t;
+    const bool valid = i < d.N;
+    unsigned spike = 0;
+    int col = -1;
+    if (valid) {
+        const unsigned info = d.info[i];
+        const int type = info & 1, region = (info >> 1) & 7, subtype = (info >> 4) & 3;
+        col = (region != PF) ? (int)(info >> 8) : -1;
+        float input = d.input[i];
+        // population-coded byte input into L4 (k is the hash order)
+        if (c->inject && region == L4) {
+            const int off = i - col * d.NPC;
+            const int b = c->byte;
+            const int ps = col * k.pref_range;
+            const bool in_r = b >= ps && b < ps + k.pref_range;
+            const float v = pm_mul(pm_mul(k.pop_gain, in_r ? k.gain_in : k.gain_out), d.gates[col].x);
+            unsigned h = (unsigned)b * 2654435761u + (unsigned)col * 0x9E3779B9u;
+            for (int q = 0; q < k.pop_k; ++q) {
+                h ^= h << 13; h ^= h >> 17; h ^= h << 5;
+                if ((int)(h % (unsigned)d.l4) == off) input = pm_add(input, v);
+            }
+        }
+        // inhibition (set after step t-1 when (t-1) % 10 == 0, cleared otherwise)
+        float inh = 0.0f;
+        if (c->inh_active) {
+            float sg = subtype == 0 ? 1.40f : subtype == 1 ? 0.85f : subtype == 2 ? 1.10f : 1.0f;
+            float rg = region == PF ? 0.60f : 1.0f;
+            float cur = pm_mul(pm_mul(pm_fma(d.fr[i], 2.0f, c->gdrive), sg), rg);
+            if (type == 1) cur = pm_mul(cur, 0.35f);
+            if (cur > 2.0f) cur = 2.0f;
+            inh = cur;
+            if (col >= 0) {
+                const int sp = d.col_sp[((t - 1) & 1) * d.ncol + col];
+                const int kk = c->kwta_k;
+                int width = kk * 8;
+                width = width < 1 ? 1 : (width > d.NPC ? d.NPC : width);
+                const int rank = (i + col * 37) % d.NPC;
+                if (sp > 0 && sp > kk && rank >= width) {
+                    float ex = pm_mul(0.35f, pm_div(pm_i2f(sp - kk), pm_i2f(kk + 1)));
+                    if (ex > 2.0f) ex = 2.0f;
+                    inh = pm_add(inh, ex);
+                }
+            }
+        }
+        // AdEx
+        int ref = d.ref[i];
+        float fr = d.fr[i];
+        float V = d.V[i];
+        unsigned short off = d.off[i];
+        if (ref > 0) {
+            ref -= 1;
+            fr = pm_mul(fr, k.fr_refr);
+            d.ref[i] = ref;
+            d.fr[i] = fr;
+        } else {
+            float s = pm_fma(d.s[i], k.syn_keep, pm_mul(input, k.syn_in));
+            float I = pm_sub(pm_add(s, d.nmda_cur[i]), inh);
+            float w = d.wad[i];
+            float ea = pm_div(pm_sub(V, k.vt), k.dT);
+            if (ea > 10.0f) ea = 10.0f;
+            if (ea < -10.0f) ea = -10.0f;
+            float et = pm_mul(k.dT, snn_expf(ea));
+            float dV = pm_mul(pm_add(pm_sub(pm_add(-V, et), w), I), k.inv_taum);
+            float dw = pm_mul(pm_fma(k.a_ad, V, -w), k.inv_tauw);
+            V = pm_add(V, dV);
+            w = pm_add(w, dw);
+            V = clampf(V, k.vmin, k.vmax);
+            float theta = pm_add(1.0f, pm_div(pm_u2f(off), 256.0f));
+            float can = d.can[i];
+            if (V >= theta) {
+                spike = 1;
+                const int last = d.last[i];
+                if (last >= 0 && t - last <= 5) atomicAdd(&d.ctrl->burst, 1ull);
+                d.last[i] = (int)t;
+                ref = k.refr_steps;
+                V = 0.0f;
+                w = pm_add(w, k.b_ad);
+                can = fminf(pm_add(can, k.ca_n_inc), 1.0f);
+                fr = pm_fma(fr, k.fr_spk_keep, k.fr_spk_add);
+                int no = (int)off + k.off_add;
+                if (no > k.off_max) no = k.off_max;
+                off = (unsigned short)no;
+            } else {
+                off = (unsigned short)pm_mul(pm_u2f(off), k.off_decay);
+                can = pm_mul(can, k.ca_n_dec);
+                fr = pm_mul(fr, k.fr_quiet);
+            }
+            d.s[i] = s;
+            d.wad[i] = w;
+            d.V[i] = V;
+            d.can[i] = can;
+            d.fr[i] = fr;
+            d.ref[i] = ref;
+            d.off[i] = off;
+        }
+        // Mg block and post trace of neuron i for this step's synapse pass
+        const float Vb = pm_fma(50.0f, V, -70.0f);
+        const float e = snn_expf(pm_div(-Vb, 16.13f));
+        d.mg[i] = pm_div(1.0f, pm_add(1.0f, pm_div(pm_mul(1.0f, e), 3.57f)));
+        float xp = pm_mul(d.xpost[i], k.dec_xpost);
+        if (spike) xp = pm_add(xp, k.a_minus);
+        d.xpost[i] = xp;
+        const unsigned hist = (d.hist[i] << 1) | spike;
+        d.hist[i] = hist;
+        // counters of this step
+        if (spike) {
+            atomicAdd(&d.ctrl->step_spikes[t & 1], 1);
+            if (i / d.per_sub < TD_DIM) atomicAdd(&d.sub_sp[(t & 1) * TD_DIM + i / d.per_sub], 1);
+            if (col >= 0) {
+                atomicAdd(&d.col_sp[(t & 1) * d.ncol + col], 1);
+                if (region == L6) atomicAdd(&d.l6_sp[(t & 1) * d.ncol + col], 1);
+            }
+            if (c->inject) {
+                atomicAdd(&d.byte_histogram[c->byte], 1);
+                atomicAdd(&d.neuron_byte_counts[(long long)i * 256 + c->byte], 1);
+            }
+            atomicAdd(&d.ctrl->ltp_visits, (unsigned long long)(d.in_ptr[i + 1] - d.in_ptr[i]));
+        }
+        // outgoing synapse groups of neuron i
+        unsigned long long arr_cnt = 0, disp_cnt = 0;
+        const int g0 = d.gbeg[i], g1 = d.gbeg[i + 1];
+        for (int g = g0; g < g1; ++g) {
+            const unsigned meta = d.gmeta[g];
+            const int dd = meta & GV_D_MASK;
+            const bool ff = meta & GV_FF, exc = meta & GV_EXC;
+            const bool arr = (hist >> dd) & 1u;
+            const bool nxt = (hist >> (dd - 1)) & 1u;
+            float4 st = d.gstate[g];  // R, u, nmda, xpre
+            if (arr && exc) st.z = pm_fma(pm_mul(k.g_nmda, st.x), st.y, st.z);
+            st.z = pm_mul(st.z, k.dec_nmda);
+            if (ff) st.x = pm_fma(pm_sub(1.0f, st.x), k.rec_ff_step, st.x);
+            st.w = pm_mul(st.w, k.dec_xpre);
+            const float x_ltp = st.w;
+            if (arr) {
+                st.w = pm_add(st.w, k.a_plus);
+                const int cl = ff ? 0 : (exc ? 1 : 2);
+                const float U = k.U[cl];
+                st.x = pm_fma(pm_sub(1.0f, st.x), k.rec[cl], st.x);
+                st.y = pm_fma(pm_sub(st.y, U), k.fac[cl], U);
+                const float un = pm_fma(U, pm_sub(1.0f, st.y), st.y);
+                const float rn = pm_mul(st.x, pm_sub(1.0f, un));
+                st.y = un > 1.0f ? 1.0f : un;
+                st.x = rn < 0.0f ? 0.0f : rn;
+                arr_cnt += (unsigned long long)d.gsize[g];
+            }
+            if (spike) disp_cnt += (unsigned long long)d.gsize[g];
+            d.gstate[g] = st;
+            const unsigned fl = (meta & (GV_D_MASK | GV_FF | GV_EXC)) | (arr ? GV_ARR : 0u) |
+                                (nxt ? GV_NEXT : 0u) | (spike ? GV_DISP : 0u);
+            d.gview[g] = make_float4(st.z, x_ltp, st.x, __uint_as_float(fl));
+        }
+        if (arr_cnt) {
+            atomicAdd(&d.ctrl->arrivals, arr_cnt);
+            atomicAdd(&d.ctrl->step_arrivals[t & 1], arr_cnt);
+        }
+        if (disp_cnt) atomicAdd(&d.ctrl->dispatched, disp_cnt);
+    }
+    // spike raster word of this warp
+    const unsigned word = __ballot_sync(0xffffffffu, spike != 0);
+    if ((threadIdx.x & 31) == 0 && (i >> 5) < d.words) {
+        const long long row = (t - c->raster_base) % d.raster_cap;
+        d.raster[row * d.words + (i >> 5)] = word;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// k_synapses: one warp per post-synaptic neuron, post-major.
+//   Ca / NMDA ....... synapse_kernels.cu:45-121
+//   LTP (post) ...... synapse_kernels.cu:153-255
+//   LTD (arrival) ... synapse_kernels.cu:257-329
+//   dispatch value .. neuron_kernels.cu:204-206 (w * R after this step's STP)
+//   input of t+1 .... neuron_kernels.cu:37-56 (delivery of the arrivals)
+//   CaMKII / elig ... synapse_kernels.cu:469-543 (every 10 steps)
+//   PSW decay ....... scheduler.cu:55-86 (every 1000 steps)
+// Both sums use the canonical order: 32-synapse chunks in ascending
+// reference synapse id, xor butterfly inside a chunk, chunks added in order.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) k_synapses(Dev d, Consts k) {
+    const int lane = threadIdx.x & 31;
+    const int j = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (j >= d.N) return;
+    const Ctrl* c = d.ctrl;
+    const long long t = c->t;
+    const float gain = c->gain;
+    const bool e0 = c->e0 != 0;
+    const bool do10 = (t % 10 == 0) && !e0;
+    const bool do1000 = (t % 1000 == 0);
+    const float prune = c->prune_thr;
+    const float Vj = d.V[j];
+    const float mgj = d.mg[j];
+    const bool post_spk = d.hist[j] & 1u;
+    const float xpost = d.xpost[j];
+    const float one_m_V = pm_sub(k.e_rev, Vj);
+    const int slot_now = (int)((t / 3) & (VAL_SLOTS - 1));
+    const int b = d.in_ptr[j], e = d.in_ptr[j + 1];
+    float acc_nmda = 0.0f, acc_in = 0.0f;
+    for (int base = b; base < e; base += 32) {
+        const int p = base + lane;
+        float term_nmda = 0.0f, term_in = 0.0f;
+        if (p < e) {
+            const unsigned g = d.gid[p];
+            const float4 v = d.gview[g];
+            const unsigned fl = __float_as_uint(v.w);
+            const bool ff = fl & GV_FF, exc = fl & GV_EXC;
+            const int dd = fl & GV_D_MASK;
+            float ca = 0.0f;
+            if (exc) {
+                ca = d.ca[p];
+                ca = pm_mul(ca, ff ? k.dec_ca_ff : k.dec_ca);
+                const float nm = pm_mul(v.x, mgj);
+                ca = pm_fma(nm, k.ca_gain, ca);
+                const float cmax = ff ? k.ca_max_ff : k.ca_max;
+                if (ca > cmax) ca = cmax;
+                d.ca[p] = ca;
+                const float I = pm_mul(pm_mul(nm, one_m_V), k.i_gain);
+                if (fabsf(I) > k.i_min) term_nmda = I;
+            }
+            const bool arr = fl & GV_ARR, disp = fl & GV_DISP, nxt = fl & GV_NEXT;
+            const bool touch = post_spk || arr || disp || do10 || do1000;
+            if (nxt && dd >= 2) {
+                const int sl = (int)(((t + 1 - dd) / 3) & (VAL_SLOTS - 1));
+                term_in = d.val[(long long)p * VAL_SLOTS + sl];
+            }
+            if (touch) {
+                float4 q = d.ev[p];  // alpha, beta, auto, elig
+                bool dirty = false;
+                const float eta = ff ? k.eta_ff : k.eta;
+                const float M = e0 ? 1.0f : c->M[exc ? 1 : 0];  // [0] inhibitory, [1] excitatory pre
+                const float pf = e0 ? 1.0f : pm_sub(1.0f, pm_mul(0.5f, q.z));
+                if (post_spk) {  // LTP from the pre trace (dense pass, post spiked)
+                    const float dw = pm_fma(v.y, k.a_plus, 0.0f);
+                    if (dw > 0.0f) q.x = pm_fma(pm_mul(pm_mul(pm_mul(eta, dw), gain), M), pf, q.x);
+                    if (ca > k.reb_thr) {
+                        const float ex = pm_sub(ca, k.reb_thr);
+                        q.y = pm_fma(pm_mul(pm_mul(pm_mul(eta, ex), k.reb_gain), gain), M, q.y);
+                    }
+                    q.w = pm_add(q.w, dw);
+                    dirty = true;
+                }
+                if (arr) {  // LTD at arrival from the post trace
+                    const float dw = pm_mul(-xpost, k.a_minus);
+                    if (dw < 0.0f) q.y = pm_fma(pm_mul(pm_mul(pm_mul(eta, -dw), gain), M), pf, q.y);
+                    q.w = pm_add(q.w, dw);
+                    dirty = true;
+                }
+                if (disp) {  // value this dispatch delivers d steps later
+                    const float wm = pm_div(pm_mul(k.w_max, q.x), pm_add(q.x, q.y));
+                    const float val = pm_mul(exc ? wm : -wm, v.z);
+                    if (dd == 1) term_in = val;
+                    else d.val[(long long)p * VAL_SLOTS + slot_now] = val;
+                }
+                if (do10) {
+                    if (exc) {
+                        float act = d.act[p], au = q.z;
+                        const float ca4 = pm_mul(pm_mul(pm_mul(ca, ca), ca), ca);
+                        const float da = pm_fma(pm_mul(k.ck_k1, ca4), pm_sub(1.0f, act),
+                                                -pm_mul(pm_mul(k.ck_k2, act), k.ck_pp1));
+                        const float du = pm_fma(pm_mul(pm_mul(k.ck_k3, act), act), pm_sub(1.0f, au),
+                                                -pm_mul(pm_mul(k.ck_k4, au), k.ck_pp1));
+                        act = clampf(pm_fma(da, k.ck_dt, act), 0.0f, 1.0f);
+                        au = clampf(pm_fma(du, k.ck_dt, au), 0.0f, 1.0f);
+                        d.act[p] = act;
+                        q.z = au;
+                    }
+                    const float a1 = pm_fma(d.e1[p], k.e1_dec, q.w);
+                    const float a2 = pm_fma(d.e2[p], k.e2_dec, a1);
+                    d.e1[p] = a1;
+                    d.e2[p] = a2;
+                    q.w = 0.0f;
+                    dirty = true;
+                }
+                if (do1000) {
+                    float a = pm_mul(q.x, k.psw_decay), bb = pm_mul(q.y, k.psw_decay);
+                    if (a < k.ab_min) a = k.ab_min;
+                    if (bb < k.ab_min) bb = k.ab_min;
+                    if (pm_add(a, bb) < prune) { a = k.ab_reset; bb = k.ab_reset; }
+                    q.x = a;
+                    q.y = bb;
+                    dirty = true;
+                }
+                if (dirty) d.ev[p] = q;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) {
+            term_nmda = pm_add(term_nmda, __shfl_xor_sync(0xffffffffu, term_nmda, o));
+            term_in = pm_add(term_in, __shfl_xor_sync(0xffffffffu, term_in, o));
+        }
+        acc_nmda = pm_add(acc_nmda, term_nmda);
+        acc_in = pm_add(acc_in, term_in);
+    }
+    if (lane == 0) {
+        d.nmda_cur[j] = acc_nmda;
+        d.input[j] = acc_in;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host engine
+// ---------------------------------------------------------------------------
+struct Engine2e : snnb::Engine {
+    snn_config cfg;
+    cudaStream_t stream = nullptr;
+    HostNet net;
+    Layout lay;
+    Consts K{};
+    Dev D{};
+    bool built = false;
+    long long steps = 0;
+    int raster_cap = 1024;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t graph_exec = nullptr;
+    int graph_steps = 0;
+    // profiling: events around every kernel (3 kernels per step)
+    bool profiling = false;
+    std::vector<cudaEvent_t> pev;
+    snn_profile prof{};
+    // device buffers
+    snnb::DevBuf<float> V, wad, s, fr, can, xpost, mg, input, nmda_cur, ca, act, e1, e2, val;
+    snnb::DevBuf<int> last, ref, gbeg, in_ptr, gsize, col_sp, l6_sp, sub_sp, byte_histogram,
+        neuron_byte_counts;
+    snnb::DevBuf<unsigned short> off;
+    snnb::DevBuf<unsigned> info, hist, gmeta, gid, byte_hist_nov, raster;
+    snnb::DevBuf<float4> gstate, gview, ev, gates;
+    snnb::DevBuf<float> w_value, w_pred, baseline;
+    snnb::DevBuf<Ctrl> ctrl;
+    snnb::DevBuf<unsigned char> corpus;
+    snnb::DevBuf<int> counts_tmp;
+
+    explicit Engine2e(const snn_config& c) : cfg(c) {
+        if (cfg.raster_steps > 0) raster_cap = cfg.raster_steps;
+        SNN_CUDA(cudaSetDevice(cfg.device));
+        SNN_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+        set_consts();
+    }
+    ~Engine2e() override {
+        for (auto e : pev) cudaEventDestroy(e);
+        if (graph_exec) cudaGraphExecDestroy(graph_exec);
+        if (graph) cudaGraphDestroy(graph);
+        if (stream) {
+            cudaStreamSynchronize(stream);
+            cudaStreamDestroy(stream);
+        }
+    }
+
+    void set_consts() {
+        Consts& k = K;
+        // ref preset: literals of src/stage2e/neuron_kernels.cu:92-160 and
+        // src/stage2e/config.h:100-303
+        k.syn_keep = 0.7f; k.syn_in = 0.3f; k.vt = 0.8f; k.dT = 0.1f;
+        k.inv_taum = pm_div(1.0f, 9.37f); k.a_ad = 0.0133f; k.inv_tauw = pm_div(1.0f, 144.0f);
+        k.b_ad = 0.0805f; k.vmin = -0.5f; k.vmax = 1.5f;
+        k.ca_n_inc = 0.2f; k.ca_n_dec = pm_sub(1.0f, pm_div(1.0f, 50.0f));
+        k.fr_refr = 0.99f; k.fr_spk_keep = 0.9f; k.fr_spk_add = 0.1f; k.fr_quiet = 0.995f;
+        k.off_decay = 0.999f; k.refr_steps = 2;
+        k.off_add = (int)pm_mul(0.001f, 256.0f); k.off_max = (int)pm_mul(0.3f, 256.0f);
+        k.dec_nmda = snn_expf(pm_div(-1.0f, 150.0f));
+        k.dec_ca = snn_expf(pm_div(-1.0f, 50.0f));
+        k.dec_ca_ff = snn_expf(pm_div(-1.0f, 10.0f));
+        k.ca_max = 1.0f; k.ca_max_ff = 0.12f;
+        k.rec_ff_step = pm_sub(1.0f, snn_expf(pm_div(-1.0f, 3.0f)));
+        k.dec_xpre = snn_expf(pm_div(-1.0f, 20.0f));
+        k.dec_xpost = snn_expf(pm_div(-1.0f, 20.0f));
+        k.g_nmda = 0.5f; k.ca_gain = 1000.0f; k.e_rev = 1.4f; k.i_gain = 0.05f; k.i_min = 1e-6f;
+        const float taus_f[NCLASS] = {200.0f, 200.0f, 200.0f}, taus_r[NCLASS] = {3.0f, 500.0f, 500.0f};
+        const float Us[NCLASS] = {0.02f, 0.2f, 0.05f};
+        for (int q = 0; q < NCLASS; ++q) {
+            k.U[q] = Us[q];
+            k.fac[q] = snn_expf(pm_div(-1.0f, taus_f[q]));
+            k.rec[q] = pm_sub(1.0f, snn_expf(pm_div(-1.0f, taus_r[q])));
+        }
+        k.a_plus = 0.03f; k.a_minus = 0.03f; k.w_max = 1.5f; k.eta = 20.0f; k.eta_ff = 2.0f;
+        k.reb_thr = 0.15f; k.reb_gain = 0.5f; k.ab_min = 1e-4f; k.ab_reset = 0.05f; k.psw_decay = 0.95f;
+        k.e1_dec = snn_expf(pm_div(-10.0f, 20.0f));
+        k.e2_dec = snn_expf(pm_div(-10.0f, 200.0f));
+        k.ck_k1 = 0.8f; k.ck_k2 = 0.1f; k.ck_k3 = 0.5f; k.ck_k4 = 0.05f; k.ck_pp1 = 0.5f; k.ck_dt = 10.0f;
+        k.mod_dec[0] = snn_expf(pm_div(-100.0f, 100.0f));
+        k.mod_dec[1] = snn_expf(pm_div(-100.0f, 200.0f));
+        k.mod_dec[2] = snn_expf(pm_div(-100.0f, 150.0f));
+        k.mod_dec[3] = snn_expf(pm_div(-100.0f, 300.0f));
+        k.rec_da[0] = -0.3f; k.rec_da[1] = 0.5f;  // [0] inhibitory pre, [1] excitatory pre
+        k.rec_ach = 0.3f;
+        k.rec_ne = pm_div(pm_u2f((unsigned)pm_mul(0.3f, 127.0f)), 127.0f);
+        k.rec_ht5 = k.rec_ne;
+        k.pop_gain = 80.0f; k.gain_in = 2.0f; k.gain_out = 0.03f; k.pop_k = 100; k.inject_interval = 3;
+    }
+
+    void build(const snn_topology_spec& spec) override {
+        SNN_REQUIRE(!built, SNN_ERR_STATE, "network already built");
+        SNN_REQUIRE(spec.rule == 0, SNN_ERR_UNSUPPORTED, "stage2e supports the reference rule only");
+        generate_reference(spec, net);
+        build_layout(net, lay);
+        K.pref_range = 256 / net.ncol;
+        const int N = net.N;
+        const int64_t S = net.S, G = lay.G;
+        D.N = N; D.N_assoc = net.N_assoc; D.NPC = net.NPC; D.ncol = net.ncol; D.l4 = net.l4;
+        D.per_sub = N / TD_DIM;
+        SNN_REQUIRE(D.per_sub > 0, SNN_ERR_ARG, "network too small for the 200-dim value function");
+        D.words = (N + 31) / 32;
+        D.raster_cap = raster_cap;
+        // neurons
+        V.alloc(N); wad.alloc(N); s.alloc(N); fr.alloc(N); can.alloc(N); xpost.alloc(N); mg.alloc(N);
+        input.alloc(N); nmda_cur.alloc(N); last.alloc(N); ref.alloc(N); off.alloc(N); info.alloc(N);
+        hist.alloc(N); gbeg.alloc(N + 1); in_ptr.alloc(N + 1);
+        for (auto* b : {&V, &wad, &s, &fr, &can, &xpost, &mg, &input, &nmda_cur}) b->zero(stream);
+        ref.zero(stream); off.zero(stream); hist.zero(stream);
+        std::vector<int> h_last(N, -1000);
+        last.upload(h_last.data(), N, stream);
+        std::vector<unsigned> h_info(N);
+        for (int i = 0; i < N; ++i) {
+            unsigned colf = net.column[i] < 0 ? 0xffffffu : (unsigned)net.column[i];
+            h_info[i] = (unsigned)net.type[i] | ((unsigned)net.region[i] << 1) |
+                        ((unsigned)net.subtype[i] << 4) | (colf << 8);
+        }
+        info.upload(h_info.data(), N, stream);
+        gbeg.upload(lay.gbeg.data(), N + 1, stream);
+        in_ptr.upload(lay.in_ptr.data(), N + 1, stream);
+        // groups
+        gmeta.alloc(G); gsize.alloc(G); gstate.alloc(G); gview.alloc(G);
+        gmeta.upload(lay.gmeta.data(), G, stream);
+        gsize.upload(lay.gsize.data(), G, stream);
+        std::vector<float4> h_gs(G);
+        for (int64_t g = 0; g < G; ++g) h_gs[g] = make_float4(1.0f, lay.gu0[g], 0.0f, 0.0f);
+        gstate.upload(h_gs.data(), G, stream);
+        gview.zero(stream);
+        // synapses, post-major
+        gid.alloc(S); ca.alloc(S); ev.alloc(S); act.alloc(S); e1.alloc(S); e2.alloc(S);
+        val.alloc((size_t)S * VAL_SLOTS);
+        gid.upload(lay.gid_pm.data(), S, stream);
+        {
+            std::vector<float4> h_ev(S);
+            for (int64_t p = 0; p < S; ++p) {
+                int32_t sid = lay.perm[p];
+                h_ev[p] = make_float4(net.alpha[sid], net.beta[sid], 0.0f, 0.0f);
+            }
+            ev.upload(h_ev.data(), S, stream);
+            SNN_CUDA(cudaStreamSynchronize(stream));
+        }
+        ca.zero(stream); act.zero(stream); e1.zero(stream); e2.zero(stream); val.zero(stream);
+        // control
+        ctrl.alloc(1);
+        Ctrl h{};
+        h.byte_override = -1;
+        h.learn = 1;
+        h.e0 = cfg.e0;
+        h.phase_offset = cfg.phase_offset;
+        ctrl.upload(&h, 1, stream);
+        gates.alloc(net.ncol);
+        std::vector<float4> h_g(net.ncol, make_float4(0.5f, 0.0f, 0.0f, 0.0f));
+        gates.upload(h_g.data(), net.ncol, stream);
+        col_sp.alloc(2 * net.ncol); l6_sp.alloc(2 * net.ncol); sub_sp.alloc(2 * TD_DIM);
+        col_sp.zero(stream); l6_sp.zero(stream); sub_sp.zero(stream);
+        byte_hist_nov.alloc(256); byte_hist_nov.zero(stream);
+        byte_histogram.alloc(256); byte_histogram.zero(stream);
+        neuron_byte_counts.alloc((size_t)N * 256); neuron_byte_counts.zero(stream);
+        w_value.alloc(TD_DIM); w_pred.alloc(TD_DIM); baseline.alloc(TD_DIM);
+        w_value.zero(stream); w_pred.zero(stream); baseline.zero(stream);
+        raster.alloc((size_t)raster_cap * D.words); raster.zero(stream);
+        corpus.alloc(1);
+        counts_tmp.alloc(1);
+        fill_dev();
+        SNN_CUDA(cudaStreamSynchronize(stream));
+        built = true;
+    }
+
+    void fill_dev() {
+        D.V = V.p; D.wad = wad.p; D.s = s.p; D.fr = fr.p; D.can = can.p; D.xpost = xpost.p; D.mg = mg.p;
+        D.input = input.p; D.nmda_cur = nmda_cur.p; D.last = last.p; D.ref = ref.p; D.off = off.p;
+        D.info = info.p; D.hist = hist.p; D.gbeg = gbeg.p; D.in_ptr = in_ptr.p;
+        D.gmeta = gmeta.p; D.gsize = gsize.p; D.gstate = gstate.p; D.gview = gview.p;
+        D.gid = gid.p; D.ca = ca.p; D.ev = ev.p; D.act = act.p; D.e1 = e1.p; D.e2 = e2.p; D.val = val.p;
+        D.ctrl = ctrl.p; D.gates = gates.p; D.col_sp = col_sp.p; D.l6_sp = l6_sp.p; D.sub_sp = sub_sp.p;
+        D.byte_hist_nov = byte_hist_nov.p; D.byte_histogram = byte_histogram.p;
+        D.neuron_byte_counts = neuron_byte_counts.p; D.w_value = w_value.p; D.w_pred = w_pred.p;
+        D.baseline = baseline.p; D.corpus = corpus.p; D.raster = raster.p;
+    }
+
+    void set_corpus(const uint8_t* b, int64_t n) override {
+        SNN_REQUIRE(built, SNN_ERR_STATE, "build the network first");
+        SNN_REQUIRE(n >= 0 && (n == 0 || b), SNN_ERR_ARG, "bad corpus");
+        if ((size_t)n > corpus.n) {
+            SNN_CUDA(cudaStreamSynchronize(stream));
+            corpus.alloc(n);
+            D.corpus = corpus.p;
+            drop_graph();
+        }
+        if (n > 0) corpus.upload(b, n, stream);
+        long long len = n, pos = 0;
+        SNN_CUDA(cudaMemcpyAsync((char*)ctrl.p + offsetof(Ctrl, corpus_len), &len, sizeof(len),
+                                 cudaMemcpyHostToDevice, stream));
+        SNN_CUDA(cudaMemcpyAsync((char*)ctrl.p + offsetof(Ctrl, corpus_pos), &pos, sizeof(pos),
+                                 cudaMemcpyHostToDevice, stream));
+        SNN_CUDA(cudaStreamSynchronize(stream));
+    }
+
+    void drop_graph() {
+        if (graph_exec) cudaGraphExecDestroy(graph_exec);
+        if (graph) cudaGraphDestroy(graph);
+        graph_exec = nullptr;
+        graph = nullptr;
+        graph_steps = 0;
+    }
+
+    // one step; with profiling, events ev[0..3] bracket the three kernels
+    // (inside a stream capture the records must be "external" so that they
+    // become event-record nodes that time the graph's kernels)
+    void launch_step(cudaStream_t st, cudaEvent_t* ev = nullptr, bool capturing = false) {
+        const int nb = (D.N + 255) / 256;
+        const long long warps = D.N;
+        const unsigned fl = capturing ? cudaEventRecordExternal : cudaEventRecordDefault;
+        if (ev) SNN_CUDA(cudaEventRecordWithFlags(ev[0], st, fl));
+        k_control<<<1, 256, 0, st>>>(D, K);
+        if (ev) SNN_CUDA(cudaEventRecordWithFlags(ev[1], st, fl));
+        k_neurons<<<nb, 256, 0, st>>>(D, K);
+        if (ev) SNN_CUDA(cudaEventRecordWithFlags(ev[2], st, fl));
+        k_synapses<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(D, K);
+        if (ev) SNN_CUDA(cudaEventRecordWithFlags(ev[3], st, fl));
+    }
+
+    void ensure_events(int n_steps) {
+        size_t need = (size_t)n_steps * 3 + 1;
+        while (pev.size() < need) {
+            cudaEvent_t e;
+            SNN_CUDA(cudaEventCreate(&e));
+            pev.push_back(e);
+        }
+    }
+
+    // accumulate the profile of n steps whose events are pev[0 .. 3n]
+    void harvest(int n) {
+        SNN_CUDA(cudaStreamSynchronize(stream));
+        for (int q = 0; q < n; ++q) {
+            for (int kk = 0; kk < 3; ++kk) {
+                float ms = 0.0f;
+                SNN_CUDA(cudaEventElapsedTime(&ms, pev[3 * q + kk], pev[3 * q + kk + 1]));
+                prof.kernel_ms[kk] += ms;
+                prof.launches[kk] += 1;
+                prof.step_ms += ms;
+            }
+        }
+        prof.steps += n;
+    }
+
+    // a graph of `n` steps (kernels read the step from device memory)
+    void ensure_graph(int n) {
+        if (graph_exec && graph_steps == n) return;
+        drop_graph();
+        if (profiling) ensure_events(n);
+        SNN_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+        for (int q = 0; q < n; ++q) launch_step(stream, profiling ? &pev[3 * q] : nullptr, true);
+        SNN_CUDA(cudaStreamEndCapture(stream, &graph));
+        SNN_CUDA(cudaGraphInstantiate(&graph_exec, graph, 0));
+        graph_steps = n;
+    }
+
+    void set_profiling(int32_t en) override {
+        SNN_REQUIRE(built, SNN_ERR_STATE, "build the network first");
+        SNN_CUDA(cudaStreamSynchronize(stream));
+        profiling = en != 0;
+        drop_graph();
+        memset(&prof, 0, sizeof(prof));
+        prof.n_kernels = 3;
+        strcpy(prof.names[0], "k_control");
+        strcpy(prof.names[1], "k_neurons");
+        strcpy(prof.names[2], "k_synapses");
+    }
+
+    void get_profile(snn_profile* o) override { *o = prof; }
+
+    void set_ctrl_field(size_t off_b, const void* v, size_t n) {
+        SNN_CUDA(cudaMemcpyAsync((char*)ctrl.p + off_b, v, n, cudaMemcpyHostToDevice, stream));
+    }
+
+    void run(int32_t n_steps, int32_t byte_override, int32_t learn, uint32_t* raster_out,
+             int32_t* counts_out) override {
+        SNN_REQUIRE(built, SNN_ERR_STATE, "build the network first");
+        SNN_REQUIRE(n_steps >= 0, SNN_ERR_ARG, "negative step count");
+        if (n_steps == 0) return;
+        int lr = learn ? 1 : 0;
+        set_ctrl_field(offsetof(Ctrl, learn), &lr, sizeof(int));
+        long long rb = steps;
+        set_ctrl_field(offsetof(Ctrl, raster_base), &rb, sizeof(rb));
+        if (byte_override >= 0) {
+            SNN_REQUIRE(byte_override < 256, SNN_ERR_ARG, "byte out of range");
+            set_ctrl_field(offsetof(Ctrl, byte_override), &byte_override, sizeof(int));
+        }
+        int done = 0;
+        const int chunk = 50;
+        while (done < n_steps) {
+            int left = n_steps - done;
+            // raster rows wrap every raster_cap steps: drain before overwriting
+            int span = std::min(left, raster_cap - (done % raster_cap));
+            int q = 0;
+            while (q < span) {
+                if (span - q >= chunk) {
+                    ensure_graph(chunk);
+                    SNN_CUDA(cudaGraphLaunch(graph_exec, stream));
+                    if (profiling) harvest(chunk);
+                    q += chunk;
+                } else {
+                    if (profiling) ensure_events(1);
+                    launch_step(stream, profiling ? &pev[0] : nullptr);
+                    SNN_CUDA(cudaGetLastError());
+                    if (profiling) harvest(1);
+                    q += 1;
+                }
+            }
+            if (raster_out || counts_out) {
+                const long long row0 = (done % raster_cap);
+                if (raster_out)
+                    SNN_CUDA(cudaMemcpyAsync(raster_out + (size_t)done * D.words,
+                                             raster.p + row0 * D.words,
+                                             (size_t)span * D.words * sizeof(unsigned),
+                                             cudaMemcpyDeviceToHost, stream));
+                if (counts_out) {
+                    std::vector<unsigned> tmp((size_t)span * D.words);
+                    SNN_CUDA(cudaMemcpyAsync(tmp.data(), raster.p + row0 * D.words,
+                                             tmp.size() * sizeof(unsigned), cudaMemcpyDeviceToHost,
+                                             stream));
+                    SNN_CUDA(cudaStreamSynchronize(stream));
+                    for (int r = 0; r < span; ++r) {
+                        int cnt = 0;
+                        for (int w = 0; w < D.words; ++w) cnt += __builtin_popcount(tmp[(size_t)r * D.words + w]);
+                        counts_out[done + r] = cnt;
+                    }
+                }
+                SNN_CUDA(cudaStreamSynchronize(stream));
+            }
+            done += span;
+        }
+        steps += n_steps;
+        SNN_CUDA(cudaGetLastError());
+    }
+
+    void sync() override { SNN_CUDA(cudaStreamSynchronize(stream)); }
+    int64_t steps_done() const override { return steps; }
+
+    void counters(snn_counters* o) override {
+        SNN_REQUIRE(built, SNN_ERR_STATE, "build the network first");
+        Ctrl h;
+        SNN_CUDA(cudaMemcpyAsync(&h, ctrl.p, sizeof(Ctrl), cudaMemcpyDeviceToHost, stream));
+        SNN_CUDA(cudaStreamSynchronize(stream));
+        memset(o, 0, sizeof(*o));
+        o->step = steps;
+        o->total_spikes = h.total_spikes + (steps > 0 ? h.step_spikes[(steps - 1) & 1] : 0);
+        o->arrivals = (int64_t)h.arrivals;
+        o->dispatched = (int64_t)h.dispatched;
+        o->dropped_ref = (int64_t)h.dropped_ref;
+        if (steps > 0 && h.step_arrivals[(steps - 1) & 1] > 750000ull)
+            o->dropped_ref += (int64_t)(h.step_arrivals[(steps - 1) & 1] - 750000ull);
+        o->ltp_visits = (int64_t)h.ltp_visits;
+        o->burst_spikes = (int64_t)h.burst;
+        o->n_neurons = net.N;
+        o->n_synapses = net.S;
+        o->n_groups = lay.G;
+        o->last_spikes = steps > 0 ? h.step_spikes[(steps - 1) & 1] : 0;
+        o->last_byte = steps > 0 ? h.byte : -1;
+        o->modeled_bytes = modeled_bytes(steps, (double)h.arrivals, (double)h.dispatched,
+                                         (double)h.ltp_visits);
+    }
+
+    // Algorithmic HBM bytes of `n` steps under this layout:
+    // dense per step: group id 4*S + Ca read/write 8*S_exc; events: dispatch
+    // 16 (alpha,beta read; value write 4 + ring sector), arrival 24 (value
+    // read 4, alpha/beta/auto/elig read+write 32 shared with LTD), LTP 32.
+    double modeled_bytes(long long n, double arr, double disp, double ltp) const {
+        double s_exc = 0;
+        for (int64_t g = 0; g < lay.G; ++g)
+            if (lay.gmeta[g] & GV_EXC) s_exc += lay.gsize[g];
+        const double S = (double)net.S;
+        double dense = n * (4.0 * S + 8.0 * s_exc);
+        double periodic = (double)((n + 9) / 10) * (S * (16.0 + 8.0 + 8.0) + s_exc * 8.0) +
+                          (double)((n + 999) / 1000) * S * 16.0;
+        double events = disp * 12.0 + arr * (4.0 + 32.0) + ltp * 32.0;
+        return dense + periodic + events;
+    }
+
+    void get_spikes(uint32_t* words, int64_t n_words) override {
+        SNN_REQUIRE(built && steps > 0, SNN_ERR_STATE, "no step executed yet");
+        SNN_REQUIRE(n_words >= D.words, SNN_ERR_ARG, "bitmask buffer too small");
+        const long long row = (steps - 1) % raster_cap;
+        SNN_CUDA(cudaMemcpyAsync(words, raster.p + row * D.words, D.words * sizeof(unsigned),
+                                 cudaMemcpyDeviceToHost, stream));
+        SNN_CUDA(cudaStreamSynchronize(stream));
+    }
+
+    template <typename T>
+    std::vector<T> fetch(const snnb::DevBuf<T>& b, size_t n) {
+        std::vector<T> h(n);
+        b.download(h.data(), n, stream);
+        SNN_CUDA(cudaStreamSynchronize(stream));
+        return h;
+    }
+
+    void get_state(int32_t which, void* buf, int64_t nbytes) override {
+        SNN_REQUIRE(built, SNN_ERR_STATE, "build the network first");
+        const int N = net.N;
+        const int64_t S = net.S;
+        auto need = [&](int64_t bytes) {
+            SNN_REQUIRE(nbytes >= bytes, SNN_ERR_ARG, "state buffer too small");
+        };
+        auto neuron_f = [&](const snnb::DevBuf<float>& b) {
+            need((int64_t)N * 4);
+            b.download((float*)buf, N, stream);
+            SNN_CUDA(cudaStreamSynchronize(stream));
+        };
+        auto neuron_i = [&](const snnb::DevBuf<int>& b) {
+            need((int64_t)N * 4);
+            b.download((int*)buf, N, stream);
+            SNN_CUDA(cudaStreamSynchronize(stream));
+        };
+        // post-major synapse array -> reference (pre-major) order
+        auto syn_pm = [&](const std::vector<float>& pm) {
+            need(S * 4);
+            float* o = (float*)buf;
+            for (int64_t p = 0; p < S; ++p) o[lay.perm[p]] = pm[p];
+        };
+        // group state -> per synapse (pre-major)
+        auto syn_group = [&](int comp) {
+            need(S * 4);
+            auto gs = fetch(gstate, lay.G);
+            float* o = (float*)buf;
+            for (int pre = 0; pre < N; ++pre) {
+                for (int32_t sid = net.row_ptr[pre]; sid < net.row_ptr[pre + 1]; ++sid) {
+                    int key = eff_delay(net.delay[sid]) * 2 + ((net.flags[sid] & RF_FF) ? 1 : 0);
+                    int g = lay.gbeg[pre];
+                    while (g < lay.gbeg[pre + 1]) {
+                        uint32_t m = lay.gmeta[g];
+                        if ((int)((m & GV_D_MASK) * 2 + ((m & GV_FF) ? 1 : 0)) == key) break;
+                        ++g;
+                    }
+                    const float4 v = gs[g];
+                    float x = comp == 0 ? v.x : comp == 1 ? v.y : comp == 2 ? v.z : v.w;
+                    // inhibitory synapses never gain NMDA conductance
+                    o[sid] = x;
+                }
+            }
+        };
+        auto ev_comp = [&](int comp) {
+            auto h = fetch(ev, S);
+            std::vector<float> pm(S);
+            for (int64_t p = 0; p < S; ++p) {
+                const float4 v = h[p];
+                pm[p] = comp == 0 ? v.x : comp == 1 ? v.y : comp == 2 ? v.z : v.w;
+            }
+            syn_pm(pm);
+        };
+        switch (which) {
+            case SNN_STATE_V: neuron_f(V); break;
+            case SNN_STATE_W_ADAPT: neuron_f(wad); break;
+            case SNN_STATE_SYN_CURRENT: neuron_f(s); break;
+            case SNN_STATE_FIRE_RATE: neuron_f(fr); break;
+            case SNN_STATE_CA_NEURON: neuron_f(can); break;
+            case SNN_STATE_INPUT: neuron_f(input); break;
+            case SNN_STATE_NMDA_CUR: neuron_f(nmda_cur); break;
+            case SNN_STATE_LAST_SPIKE: neuron_i(last); break;
+            case SNN_STATE_REFRACTORY: neuron_i(ref); break;
+            case SNN_STATE_X_POST: neuron_f(xpost); break;
+            case SNN_STATE_THRESH_OFF: {
+                need((int64_t)N * 4);
+                auto h = fetch(off, N);
+                for (int i = 0; i < N; ++i) ((int*)buf)[i] = h[i];
+                break;
+            }
+            case SNN_STATE_ALPHA: ev_comp(0); break;
+            case SNN_STATE_BETA: ev_comp(1); break;
+            case SNN_STATE_CAMKII_AUTO: ev_comp(2); break;
+            case SNN_STATE_ELIG: ev_comp(3); break;
+            case SNN_STATE_WEIGHT: {
+                auto h = fetch(ev, S);
+                std::vector<float> pm(S);
+                for (int64_t p = 0; p < S; ++p) {
+                    float m = pm_div(pm_mul(1.5f, h[p].x), pm_add(h[p].x, h[p].y));
+                    pm[p] = (net.flags[lay.perm[p]] & (RF_AMPA | RF_NMDA)) ? m : -m;
+                }
+                syn_pm(pm);
+                break;
+            }
+            case SNN_STATE_CA: syn_pm(fetch(ca, S)); break;
+            case SNN_STATE_CAMKII_ACT: syn_pm(fetch(act, S)); break;
+            case SNN_STATE_E1: syn_pm(fetch(e1, S)); break;
+            case SNN_STATE_E2: syn_pm(fetch(e2, S)); break;
+            case SNN_STATE_RESOURCE: syn_group(0); break;
+            case SNN_STATE_UTIL: syn_group(1); break;
+            case SNN_STATE_NMDA_G: syn_group(2); break;
+            case SNN_STATE_X_PRE: syn_group(3); break;
+            case SNN_STATE_POST: need(S * 4); memcpy(buf, net.post.data(), S * 4); break;
+            case SNN_STATE_DELAY: need(S); memcpy(buf, net.delay.data(), S); break;
+            case SNN_STATE_FLAGS: need(S); memcpy(buf, net.flags.data(), S); break;
+            case SNN_STATE_ROW_PTR: need((int64_t)(N + 1) * 4); memcpy(buf, net.row_ptr.data(), (N + 1) * 4); break;
+            case SNN_STATE_GATES: {
+                need((int64_t)net.ncol * 16);
+                gates.download((float4*)buf, net.ncol, stream);
+                SNN_CUDA(cudaStreamSynchronize(stream));
+                break;
+            }
+            case SNN_STATE_MODULATORS: {
+                need(16);
+                Ctrl h;
+                ctrl.download(&h, 1, stream);
+                SNN_CUDA(cudaStreamSynchronize(stream));
+                memcpy(buf, h.conc, 16);
+                break;
+            }
+            case SNN_STATE_BYTE_HIST: {
+                need(256 * 4);
+                byte_histogram.download((int*)buf, 256, stream);
+                SNN_CUDA(cudaStreamSynchronize(stream));
+                break;
+            }
+            case SNN_STATE_NEURON_BYTE_COUNTS: {
+                need((int64_t)N * 256 * 4);
+                neuron_byte_counts.download((int*)buf, (size_t)N * 256, stream);
+                SNN_CUDA(cudaStreamSynchronize(stream));
+                break;
+            }
+            default: throw snnb::Error(SNN_ERR_ARG, "unknown state field");
+        }
+    }
+
+    void set_e0(int32_t en) override {
+        SNN_REQUIRE(built, SNN_ERR_STATE, "build the network first");
+        int v = en ? 1 : 0;
+        set_ctrl_field(offsetof(Ctrl, e0), &v, sizeof(int));
+        SNN_CUDA(cudaStreamSynchronize(stream));
+    }
+
+    void save(const char*, int32_t) override {
+        throw snnb::Error(SNN_ERR_UNSUPPORTED, "stage2e save not implemented yet");
+    }
+    void load(const char*, int32_t) override {
+        throw snnb::Error(SNN_ERR_UNSUPPORTED, "stage2e load not implemented yet");
+    }
+};
+
+}  // namespace snn2e
+
+namespace snnb {
+Engine* make_engine_stage2e(const snn_config& cfg) { return new snn2e::Engine2e(cfg); }
+}  // namespace snnb

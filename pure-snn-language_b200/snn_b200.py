@@ -1,0 +1,275 @@
+"""Python binding of the B200 SNN core (libsnn_b200.so, C ABI in
+include/snn_b200.h).
+
+Mirrors the reference host API (TSOFTP-afk/pure-snn-language):
+``Network`` plays the role of ``stage2e::BioMechanismScheduler`` +
+``MemoryAllocator`` (src/stage2e/scheduler.cuh:66-224) and of
+``SNNNetwork`` (src/include/network.h:11-95): build by columns and layers,
+step / run with byte injection, read state and counters, save / load.
+
+The library must be built (``make -C pure-snn-language_b200``); importing this
+module on a machine without the built library, or creating a network without
+a CUDA device, raises instead of falling back to anything else.
+"""
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libsnn_b200.so")
+
+SNN_OK = 0
+ERRORS = {1: "SNN_ERR_ARG", 2: "SNN_ERR_CUDA", 3: "SNN_ERR_OOM", 4: "SNN_ERR_STATE",
+          5: "SNN_ERR_IO", 6: "SNN_ERR_UNSUPPORTED", 7: "SNN_ERR_NO_DEVICE"}
+MODEL_STAGE2E, MODEL_STAGE0 = 0, 1
+PRESET_REF, PRESET_BASELINE = 0, 1
+FMT_NATIVE, FMT_SNN2_V1, FMT_SCKP_V2, FMT_RAW_F32 = 0, 1, 2, 3
+
+STATE = {
+    "V": (0, np.float32, "N"), "w": (1, np.float32, "N"), "s": (2, np.float32, "N"),
+    "fr": (3, np.float32, "N"), "ca_neuron": (4, np.float32, "N"),
+    "input": (5, np.float32, "N"), "nmda_cur": (6, np.float32, "N"),
+    "last": (7, np.int32, "N"), "ref": (8, np.int32, "N"), "x_post": (9, np.float32, "N"),
+    "thresh_off": (10, np.int32, "N"),
+    "alpha": (20, np.float32, "S"), "beta": (21, np.float32, "S"),
+    "weight": (22, np.float32, "S"), "x_pre": (23, np.float32, "S"),
+    "nmda": (24, np.float32, "S"), "ca": (25, np.float32, "S"),
+    "R": (26, np.float32, "S"), "u": (27, np.float32, "S"), "elig": (28, np.float32, "S"),
+    "camkii_act": (29, np.float32, "S"), "autophos": (30, np.float32, "S"),
+    "e1": (31, np.float32, "S"), "e2": (32, np.float32, "S"),
+    "post": (40, np.int32, "S"), "delay": (41, np.uint8, "S"), "row_ptr": (42, np.int32, "N1"),
+    "flags": (43, np.uint8, "S"), "gates": (50, np.float32, "G4"),
+    "modulators": (51, np.float32, "4"), "byte_hist": (52, np.int32, "256"),
+    "neuron_byte_counts": (53, np.int32, "N256"),
+}
+
+
+class SnnError(RuntimeError):
+    def __init__(self, code, msg):
+        super().__init__(f"{ERRORS.get(code, code)}: {msg}")
+        self.code = code
+
+
+class Config(C.Structure):
+    _fields_ = [("model", C.c_int32), ("preset", C.c_int32), ("device", C.c_int32),
+                ("e0", C.c_int32), ("phase_offset", C.c_int32), ("raster_steps", C.c_int32),
+                ("reserved", C.c_int32 * 10)]
+
+
+class TopologySpec(C.Structure):
+    _fields_ = [("n_columns", C.c_int32), ("l4", C.c_int32), ("l23", C.c_int32),
+                ("l5", C.c_int32), ("l6", C.c_int32), ("pf_groups", C.c_int32),
+                ("pf_group_size", C.c_int32), ("deg_intra", C.c_int32), ("deg_inter", C.c_int32),
+                ("deg_l5_pf", C.c_int32), ("deg_pf_self", C.c_int32),
+                ("deg_pf_assoc", C.c_int32), ("total_synapses", C.c_int64),
+                ("seed", C.c_uint32), ("rule", C.c_int32), ("reserved", C.c_int32 * 8)]
+
+
+class Counters(C.Structure):
+    _fields_ = [("step", C.c_int64), ("total_spikes", C.c_int64), ("arrivals", C.c_int64),
+                ("dispatched", C.c_int64), ("dropped_ref", C.c_int64),
+                ("ltp_visits", C.c_int64), ("burst_spikes", C.c_int64),
+                ("n_neurons", C.c_int64), ("n_synapses", C.c_int64), ("n_groups", C.c_int64),
+                ("last_spikes", C.c_int32), ("last_byte", C.c_int32),
+                ("modeled_bytes", C.c_double), ("reserved", C.c_int64 * 6)]
+
+    def as_dict(self):
+        return {k: getattr(self, k) for k, _ in self._fields_ if k != "reserved"}
+
+
+class Profile(C.Structure):
+    _fields_ = [("steps", C.c_int64), ("n_kernels", C.c_int32), ("reserved0", C.c_int32),
+                ("kernel_ms", C.c_double * 8), ("launches", C.c_int64 * 8),
+                ("step_ms", C.c_double), ("names", (C.c_char * 32) * 8)]
+
+    def as_dict(self):
+        k = self.n_kernels
+        return {"steps": self.steps, "step_ms": self.step_ms,
+                "kernels": {self.names[i].value.decode(): {"ms": self.kernel_ms[i],
+                                                           "launches": self.launches[i]}
+                            for i in range(k)}}
+
+
+EXPORTS = ["snn_config_init", "snn_topology_init", "snn_create", "snn_destroy",
+           "snn_last_error", "snn_version", "snn_build_columns", "snn_set_corpus", "snn_step",
+           "snn_run", "snn_synchronize", "snn_get_spikes", "snn_get_state", "snn_get_counters",
+           "snn_set_dopamine", "snn_set_e0", "snn_save", "snn_load", "snn_stream_generate",
+           "snn_set_profiling", "snn_get_profile"]
+
+_lib = None
+
+
+def lib():
+    """Load libsnn_b200.so (raises if it was not built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise OSError(f"{LIB_PATH} is missing: build it with `make -C {HERE}`")
+        L = C.CDLL(LIB_PATH)
+        vp = C.c_void_p
+        L.snn_config_init.argtypes = [C.POINTER(Config), C.c_int32, C.c_int32]
+        L.snn_topology_init.argtypes = [C.POINTER(TopologySpec), C.c_int32, C.c_int32]
+        L.snn_create.argtypes = [C.POINTER(Config), C.POINTER(vp)]
+        L.snn_destroy.argtypes = [vp]
+        L.snn_destroy.restype = None
+        L.snn_last_error.argtypes = [vp]
+        L.snn_last_error.restype = C.c_char_p
+        L.snn_version.restype = C.c_char_p
+        L.snn_build_columns.argtypes = [vp, C.POINTER(TopologySpec)]
+        L.snn_set_corpus.argtypes = [vp, vp, C.c_int64]
+        L.snn_step.argtypes = [vp, C.c_int32, C.c_int32, C.c_int32]
+        L.snn_run.argtypes = [vp, C.c_int32, vp, C.c_int64, C.c_int32, vp, vp]
+        L.snn_synchronize.argtypes = [vp]
+        L.snn_get_spikes.argtypes = [vp, vp, C.c_int64]
+        L.snn_get_state.argtypes = [vp, C.c_int32, vp, C.c_int64]
+        L.snn_get_counters.argtypes = [vp, C.POINTER(Counters)]
+        L.snn_set_dopamine.argtypes = [vp, C.c_float]
+        L.snn_set_e0.argtypes = [vp, C.c_int32]
+        L.snn_save.argtypes = [vp, C.c_char_p, C.c_int32]
+        L.snn_load.argtypes = [vp, C.c_char_p, C.c_int32]
+        L.snn_stream_generate.argtypes = [vp, C.c_int64, C.c_uint64, C.c_double, C.c_double]
+        L.snn_set_profiling.argtypes = [vp, C.c_int32]
+        L.snn_get_profile.argtypes = [vp, C.POINTER(Profile)]
+        _lib = L
+    return _lib
+
+
+def stream(n, seed=42, p_cjk=0.452, zipf_s=1.1):
+    """Seeded synthetic UTF-8 byte stream (numpy uint8[n]).  p_cjk=0.452 is
+    the `ref45` preset (about 47.5 % continuation bytes), 0.85 is `b85`."""
+    out = np.zeros(n, np.uint8)
+    rc = lib().snn_stream_generate(out.ctypes.data, n, seed, p_cjk, zipf_s)
+    if rc:
+        raise SnnError(rc, "snn_stream_generate")
+    return out
+
+
+def byte_classes(b):
+    """Fractions of ASCII, UTF-8 head and continuation bytes."""
+    b = np.asarray(b)
+    n = max(b.size, 1)
+    return {"ascii": float((b < 0x80).sum()) / n,
+            "head": float(((b >= 0xC0) & (b < 0xF8)).sum()) / n,
+            "continuation": float(((b >= 0x80) & (b < 0xC0)).sum()) / n}
+
+
+def topology(model=MODEL_STAGE2E, n_columns=50, **overrides):
+    spec = TopologySpec()
+    rc = lib().snn_topology_init(C.byref(spec), model, n_columns)
+    if rc:
+        raise SnnError(rc, "snn_topology_init")
+    for k, v in overrides.items():
+        setattr(spec, k, v)
+    return spec
+
+
+class Network:
+    """One network on one GPU (one snn_ctx)."""
+
+    def __init__(self, model=MODEL_STAGE2E, preset=PRESET_REF, device=0, e0=False,
+                 phase_offset=0, raster_steps=1024):
+        L = lib()
+        self.L = L
+        cfg = Config()
+        self._check(L.snn_config_init(C.byref(cfg), model, preset), None)
+        cfg.device, cfg.e0, cfg.phase_offset, cfg.raster_steps = device, int(e0), phase_offset, raster_steps
+        h = C.c_void_p()
+        rc = L.snn_create(C.byref(cfg), C.byref(h))
+        if rc:
+            raise SnnError(rc, L.snn_last_error(None).decode())
+        self.h = h
+        self.model = model
+        self.N = self.S = 0
+
+    def _check(self, rc, h="self"):
+        if rc:
+            msg = self.L.snn_last_error(self.h if h == "self" else None)
+            raise SnnError(rc, msg.decode() if msg else "")
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.L.snn_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def build_columns(self, spec):
+        self._check(self.L.snn_build_columns(self.h, C.byref(spec)))
+        c = self.counters()
+        self.N, self.S = c["n_neurons"], c["n_synapses"]
+        self.words = (self.N + 31) // 32
+        self.n_columns = spec.n_columns
+        return self
+
+    def set_corpus(self, data):
+        b = np.ascontiguousarray(np.frombuffer(bytes(data), np.uint8))
+        self._check(self.L.snn_set_corpus(self.h, b.ctypes.data, b.size))
+
+    def step(self, step, inject_byte=-1, learn=True):
+        self._check(self.L.snn_step(self.h, step, inject_byte, int(learn)))
+
+    def run(self, n_steps, data=None, learn=True, raster=False, counts=False):
+        """Run n_steps; returns (raster uint32[n_steps, words] or None,
+        counts int32[n_steps] or None)."""
+        r = np.zeros((n_steps, self.words), np.uint32) if raster else None
+        c = np.zeros(n_steps, np.int32) if counts else None
+        b = None
+        if data is not None:
+            b = np.ascontiguousarray(np.frombuffer(bytes(data), np.uint8))
+        self._check(self.L.snn_run(self.h, n_steps, b.ctypes.data if b is not None else None,
+                                   b.size if b is not None else 0, int(learn),
+                                   r.ctypes.data if r is not None else None,
+                                   c.ctypes.data if c is not None else None))
+        return r, c
+
+    def synchronize(self):
+        self._check(self.L.snn_synchronize(self.h))
+
+    def spikes(self):
+        w = np.zeros(self.words, np.uint32)
+        self._check(self.L.snn_get_spikes(self.h, w.ctypes.data, w.size))
+        return np.unpackbits(w.view(np.uint8), bitorder="little")[: self.N]
+
+    def state(self, name):
+        which, dt, shape = STATE[name]
+        n = {"N": self.N, "S": self.S, "N1": self.N + 1, "4": 4, "256": 256,
+             "N256": self.N * 256, "G4": 4 * self.n_columns}[shape]
+        out = np.zeros(n, dt)
+        self._check(self.L.snn_get_state(self.h, which, out.ctypes.data, out.nbytes))
+        return out.reshape(-1, 4) if shape == "G4" else out
+
+    def counters(self):
+        c = Counters()
+        self._check(self.L.snn_get_counters(self.h, C.byref(c)))
+        return c.as_dict()
+
+    def set_profiling(self, enable=True):
+        self._check(self.L.snn_set_profiling(self.h, int(enable)))
+
+    def profile(self):
+        p = Profile()
+        self._check(self.L.snn_get_profile(self.h, C.byref(p)))
+        return p.as_dict()
+
+    def set_dopamine(self, level):
+        self._check(self.L.snn_set_dopamine(self.h, level))
+
+    def set_e0(self, enable):
+        self._check(self.L.snn_set_e0(self.h, int(enable)))
+
+    def save(self, path, fmt=FMT_NATIVE):
+        self._check(self.L.snn_save(self.h, path.encode(), fmt))
+
+    def load(self, path, fmt=FMT_NATIVE):
+        self._check(self.L.snn_load(self.h, path.encode(), fmt))
