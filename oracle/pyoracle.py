@@ -181,3 +181,108 @@ def expf_array(x):
     y = np.empty_like(x)
     lib().o2e_expf_array(x.ctypes.data, y.ctypes.data, x.size)
     return y
+
+
+# ---------------------------------------------------------------------------
+# Stage 0 / Stage 2 oracle (oracle/oracle0.cpp)
+# ---------------------------------------------------------------------------
+class O0Params(C.Structure):
+    _fields_ = [("n_columns", C.c_int32), ("n_sens", C.c_int32), ("n_assoc", C.c_int32),
+                ("n_motor", C.c_int32), ("deg_intra", C.c_int32), ("deg_inter", C.c_int32),
+                ("seed", C.c_uint32), ("w_max", C.c_float), ("input_gain", C.c_float),
+                ("homeo_lr", C.c_float), ("homeo_max", C.c_float), ("target_sa", C.c_float),
+                ("target_m", C.c_float), ("reset_interval", C.c_int32), ("dopamine", C.c_float),
+                ("n_threads", C.c_int32)]
+
+
+def stage0_params(columnar=False, baseline=True, seed=42, n_threads=0, n_columns=10):
+    """Stage 0 block network (configuration 0) or 10-column Stage 2 network
+    (configuration 1); baseline=True uses the benchmark constants, False the
+    reference Stage 2 build constants (gain 5, LR 0.005, max 0.1, 15 Hz)."""
+    p = O0Params()
+    if columnar:
+        p.n_columns, p.n_sens, p.n_assoc, p.n_motor = n_columns, 200, 600, 200
+        p.deg_intra, p.deg_inter = 80, 20
+        p.reset_interval = 10000
+    else:
+        p.n_columns, p.n_sens, p.n_assoc, p.n_motor = 0, 2000, 6000, 2000
+        p.deg_intra, p.deg_inter = 100, 0
+        p.reset_interval = 0
+    p.seed = seed
+    if baseline:
+        p.w_max, p.input_gain, p.homeo_lr, p.homeo_max = 1.0, 1.5, 1e-4, 2.0
+        p.target_sa, p.target_m = 0.005, 0.030
+    else:
+        p.w_max, p.input_gain, p.homeo_lr, p.homeo_max = 0.3, 5.0, 0.005, 0.1
+        p.target_sa, p.target_m = 0.015, 0.030
+    p.dopamine = 1.0
+    p.n_threads = n_threads
+    return p
+
+
+class Oracle0:
+    def __init__(self, params):
+        L = lib()
+        if not hasattr(L, "_o0_ready"):
+            L.o0_create.restype = C.c_void_p
+            L.o0_create.argtypes = [C.POINTER(O0Params)]
+            L.o0_destroy.argtypes = [C.c_void_p]
+            L.o0_run.argtypes = [C.c_void_p, C.c_int32, C.c_void_p]
+            L.o0_sizes.argtypes = [C.c_void_p, C.c_void_p]
+            L.o0_spikes.argtypes = [C.c_void_p, C.c_void_p]
+            L.o0_neuron.argtypes = [C.c_void_p, C.c_int32, C.c_void_p]
+            L.o0_synapse.argtypes = [C.c_void_p, C.c_int32, C.c_void_p]
+            L.o0_topology.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p]
+            L.o0_set_dopamine.argtypes = [C.c_void_p, C.c_float]
+            L._o0_ready = True
+        self.L = L
+        self.h = L.o0_create(C.byref(params))
+        sz = self.sizes()
+        self.N, self.S = int(sz[0]), int(sz[1])
+
+    def sizes(self):
+        out = np.zeros(5, np.int64)
+        self.L.o0_sizes(self.h, out.ctypes.data)
+        return out
+
+    def run(self, n, bytes_=None):
+        b = None
+        if bytes_ is not None:
+            b = np.ascontiguousarray(np.asarray(bytes_, dtype=np.int32))
+        self.L.o0_run(self.h, n, b.ctypes.data if b is not None else None)
+
+    def spikes(self):
+        out = np.zeros(self.N, np.uint8)
+        self.L.o0_spikes(self.h, out.ctypes.data)
+        return out
+
+    def neuron(self, which):
+        idx = {"V": 0, "I": 1, "fr": 2, "input": 3, "last_spk": 4, "off": 5, "ref": 6}[which]
+        out = np.zeros(self.N, np.float32)
+        self.L.o0_neuron(self.h, idx, out.ctypes.data)
+        return out
+
+    def synapse(self, which):
+        out = np.zeros(self.S, np.float32)
+        self.L.o0_synapse(self.h, {"w": 0, "elig": 1}[which], out.ctypes.data)
+        return out
+
+    def topology(self):
+        pre = np.zeros(self.S, np.int32)
+        post = np.zeros(self.S, np.int32)
+        self.L.o0_topology(self.h, pre.ctypes.data, post.ctypes.data)
+        return pre, post
+
+    def set_dopamine(self, da):
+        self.L.o0_set_dopamine(self.h, da)
+
+    def close(self):
+        if self.h:
+            self.L.o0_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

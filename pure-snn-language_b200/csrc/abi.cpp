@@ -73,9 +73,14 @@ int snn_topology_init(snn_topology_spec* spec, int32_t model, int32_t n_columns)
     if (model == SNN_MODEL_STAGE0) {
         memset(spec, 0, sizeof(*spec));
         spec->n_columns = n_columns;  // 0 = Stage 0 single block
-        if (n_columns == 0) { spec->l4 = 2000; spec->l23 = 6000; spec->l5 = 2000; }
-        else { spec->l4 = 200; spec->l23 = 600; spec->l5 = 200; }
-        spec->deg_intra = 100;
+        if (n_columns == 0) {  // Stage 0: 100 out-edges anywhere
+            spec->l4 = 2000; spec->l23 = 6000; spec->l5 = 2000;
+            spec->deg_intra = 100;
+        } else {               // Stage 2 columns: 80 intra + 20 inter out-edges
+            spec->l4 = 200; spec->l23 = 600; spec->l5 = 200;
+            spec->deg_intra = 80;
+            spec->deg_inter = 20;
+        }
         spec->seed = 42;
         spec->rule = 1;
         return SNN_OK;

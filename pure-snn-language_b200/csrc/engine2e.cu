@@ -50,6 +50,10 @@ constexpr int TD_DIM = 200;
 // group view flag bits (view.w holds them as raw bits)
 constexpr uint32_t GV_D_MASK = 0x1f, GV_FF = 1u << 5, GV_EXC = 1u << 6, GV_ARR = 1u << 7,
                    GV_NEXT = 1u << 8, GV_DISP = 1u << 9;
+constexpr int NEU_BLOCK = 128;  // k_neurons CTA size; groups carry their pre's index in it
+// packed static group word: d_eff | ff << 5 | exc << 6 | size << 8 | (pre % NEU_BLOCK) << 24
+__host__ __device__ inline unsigned gw_size(unsigned m) { return (m >> 8) & 0xffffu; }
+__host__ __device__ inline unsigned gw_lpre(unsigned m) { return m >> 24; }
 
 struct Consts {
     // neuron (normalised AdEx, src/stage2e/neuron_kernels.cu:85-165)
@@ -85,6 +89,8 @@ struct Ctrl {
     int step_spikes[2];
     unsigned long long step_arrivals[2];
     long long raster_base;  // step whose raster is in row 0
+    unsigned hist_total;    // sum of the byte history (novelty denominator)
+    int error;              // set by a kernel whose bounded wait ran out
 };
 
 struct Dev {
@@ -98,6 +104,7 @@ struct Dev {
     // groups
     unsigned* gmeta;
     int* gsize;
+    int* gpre;
     float4* gstate;  // R, u, nmda, xpre
     float4* gview;   // nmda, xpre_ltp, R_dispatch, flags
     // synapses (post-major)
@@ -118,6 +125,8 @@ struct Dev {
     unsigned* raster;
     int raster_cap, words;
     int N, N_assoc, NPC, ncol, l4, per_sub;
+    const int* tile_post;  // n_tiles + 1 post boundaries of the synapse-pass tiles
+    int n_tiles, tile_cap;  // tiles; staged elements per stream per stage
 };
 
 __device__ __forceinline__ int phase_of(long long step) {
@@ -133,139 +142,80 @@ __device__ __forceinline__ float clampf(float x, float lo, float hi) {
 }
 
 // ---------------------------------------------------------------------------
-// k_control: one CTA.  src/stage2e/scheduler.cu:485-540 (gate, byte) and the
-// deferred end-of-step host work of step t-1 (:569-670, :688-751).
+// k_control: one CTA at the start of step t.  Phase gain, byte and M_ij of
+// step t (src/stage2e/scheduler.cu:485-540, synapse_kernels.cu:207-211) and
+// the thalamic gate from the column counts of step t-1
+// (src/stage2e/thalamic_gate.cu:53-142).
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) k_control(Dev d, Consts k) {
+__global__ void __launch_bounds__(64) k_control(Dev d, Consts k) {
     Ctrl* c = d.ctrl;
     __shared__ long long s_t;
-    __shared__ int s_inject, s_byte, s_prev_ok;
+    __shared__ int s_inject, s_byte;
     __shared__ unsigned s_total_h, s_bc;
     const int tid = threadIdx.x;
     if (tid == 0) {
-        long long t = c->next_t;
-        c->t = t;
-        c->next_t = t + 1;
-        s_t = t;
-        const long long prev = t - 1;
-        s_prev_ok = prev >= 0;
-        c->inh_active = 0;
-        if (prev >= 0) {
-            const int sp_prev = c->step_spikes[prev & 1];
-            const float avg = c->total_steps > 0
-                                  ? pm_div(pm_ll2f(c->total_spikes), pm_ll2f(c->total_steps))
-                                  : 0.0f;
-            // inhibition of step prev (scheduler.cu:688-722), applied at step t
-            if (prev % 10 == 0) {
-                float drive = pm_div(pm_i2f(c->last_spikes), pm_add(avg, 1.0f));
-                drive = clampf(drive, 0.0f, 2.0f);
-                c->gdrive = pm_mul(drive, 0.15f);
-                int kk = (int)pm_mul(pm_div(avg, pm_i2f(d.ncol)), 0.5f);
-                c->kwta_k = kk < 3 ? 3 : (kk > 5 ? 5 : kk);
-                c->inh_active = 1;
-            }
-            // modulators of step prev (scheduler.cu:724-751, modulatory_kernels.cu:176-254)
-            if (prev % 100 == 0 && !c->e0) {
-                float cur = pm_i2f(c->last_spikes);
-                float nov = avg > 0.0f ? pm_div(fabsf(pm_sub(cur, avg)), pm_add(avg, 1.0f)) : 0.0f;
-                if (nov > 1.0f) nov = 1.0f;
-                float pred = (cur > 10.0f && cur < 1000.0f) ? 0.5f : 0.1f;
-                float reward = pm_add(pm_mul(0.5f, nov), pm_mul(0.3f, pred));
-                const int* sub = d.sub_sp + (prev & 1) * TD_DIM;
-                const float per = pm_i2f(d.per_sub);
-                float vs = 0.0f;
-                for (int q = 0; q < TD_DIM; ++q)
-                    vs = pm_fma(d.w_value[q], pm_div(pm_i2f(sub[q]), per), vs);
-                const float om = pm_sub(1.0f, 0.99f);
-                float vsp = 0.0f;
-                for (int q = 0; q < TD_DIM; ++q) {
-                    float f = pm_div(pm_i2f(sub[q]), per);
-                    float b = pm_fma(0.99f, d.baseline[q], pm_mul(om, f));
-                    d.baseline[q] = b;
-                    vsp = pm_fma(d.w_value[q], pm_mul(d.w_pred[q], f), vsp);
-                }
-                float delta = pm_sub(pm_add(reward, pm_mul(0.9f, vsp)), vs);
-                for (int q = 0; q < TD_DIM; ++q) {
-                    float f = pm_div(pm_i2f(sub[q]), per);
-                    d.w_value[q] = clampf(pm_fma(pm_mul(0.001f, delta), f, d.w_value[q]), -1.0f, 1.0f);
-                    float pe = pm_sub(f, d.baseline[q]);
-                    d.w_pred[q] = pm_fma(pm_mul(0.001f, pe), f, d.w_pred[q]);
-                }
-                float sig[4];
-                sig[0] = pm_add(0.1f, delta > 0.0f ? delta : pm_mul(0.3f, delta));
-                if (sig[0] < 0.0f) sig[0] = 0.0f;
-                sig[1] = pm_add(pm_add(0.2f, pm_mul(0.3f, nov)), pm_mul(0.1f, pred));
-                sig[2] = 0.05f;
-                sig[3] = 0.1f;
-                if (delta < -0.5f) sig[3] = pm_add(sig[3], pm_mul(0.3f, fabsf(delta)));
-                for (int m = 0; m < 4; ++m)
-                    c->conc[m] = clampf(pm_fma(c->conc[m], k.mod_dec[m], sig[m]), 0.0f, 2.0f);
-            }
-            // statistics of step prev (scheduler.cu:627-670)
-            c->total_steps += 1;
-            c->total_spikes += sp_prev;
-            if (prev % k.inject_interval == 0) c->inject_spikes += sp_prev;
-            c->last_spikes = sp_prev;
-            unsigned long long arr = c->step_arrivals[prev & 1];
-            if (arr > 750000ull) c->dropped_ref += arr - 750000ull;
-        }
-        // phase, byte, M_ij of step t
-        const int ph = phase_of(t + c->phase_offset);
-        c->gain = c->learn ? c_phase_gain[ph] : 0.0f;
-        c->prune_thr = c_phase_prune[ph];
+        // all loads first (independent), then the dependent byte lookups
+        const long long t = c->next_t;
+        const int phase_offset = c->phase_offset, learn = c->learn, bo = c->byte_override;
+        const int e0 = c->e0;
+        const long long clen = c->corpus_len, cpos = c->corpus_pos;
+        const float c0 = c->conc[0], c1 = c->conc[1], c2 = c->conc[2], c3 = c->conc[3];
+        const unsigned htot = c->hist_total;
         const int inj = (t % k.inject_interval) == 0;
         int byte = 0;
         if (inj) {
-            if (c->byte_override >= 0) {
-                byte = c->byte_override;
-            } else if (c->corpus_len > 0) {
-                byte = d.corpus[c->corpus_pos];
-                c->corpus_pos = (c->corpus_pos + 1) % c->corpus_len;
-            } else {
-                byte = (int)((t / k.inject_interval) % 256);
-            }
+            if (bo >= 0) byte = bo;
+            else if (clen > 0) byte = d.corpus[cpos];
+            else byte = (int)((t / k.inject_interval) % 256);
         }
+        const unsigned bc = d.byte_hist_nov[byte];
+        const int ph = phase_of(t + phase_offset);
+        float M[2];
+        for (int e = 0; e < 2; ++e) {
+            if (e0) { M[e] = 1.0f; continue; }
+            float z = pm_mul(k.rec_da[e], c0);
+            z = pm_fma(k.rec_ach, c1, z);
+            z = pm_fma(k.rec_ne, c2, z);
+            z = pm_fma(k.rec_ht5, c3, z);
+            M[e] = pm_div(1.0f, pm_add(1.0f, snn_expf(-z)));
+        }
+        c->t = t;
+        c->next_t = t + 1;
+        c->gain = learn ? c_phase_gain[ph] : 0.0f;
+        c->prune_thr = c_phase_prune[ph];
+        if (inj && bo < 0 && clen > 0) c->corpus_pos = (cpos + 1) % clen;
         c->byte_override = -1;
         c->inject = inj;
         c->byte = inj ? byte : -1;
-        s_inject = inj;
-        s_byte = byte;
-        for (int e = 0; e < 2; ++e) {
-            if (c->e0) { c->M[e] = 1.0f; continue; }
-            float z = pm_mul(k.rec_da[e], c->conc[0]);
-            z = pm_fma(k.rec_ach, c->conc[1], z);
-            z = pm_fma(k.rec_ne, c->conc[2], z);
-            z = pm_fma(k.rec_ht5, c->conc[3], z);
-            c->M[e] = pm_div(1.0f, pm_add(1.0f, snn_expf(-z)));
-        }
-        unsigned tot = 0;
-        for (int b = 0; b < 256; ++b) tot += d.byte_hist_nov[b];
-        s_total_h = tot;
-        s_bc = d.byte_hist_nov[byte];
-        // fresh per-step counters for step t
+        c->M[0] = M[0];
+        c->M[1] = M[1];
         c->step_spikes[t & 1] = 0;
         c->step_arrivals[t & 1] = 0ull;
+        s_t = t;
+        s_inject = inj;
+        s_byte = byte;
+        s_total_h = htot;
+        s_bc = bc;
     }
     __syncthreads();
     const long long t = s_t;
-    // zero this step's column / sub-column counters
+    const bool prev_ok = t > 0;
     for (int q = tid; q < d.ncol; q += blockDim.x) {
         d.col_sp[(t & 1) * d.ncol + q] = 0;
         d.l6_sp[(t & 1) * d.ncol + q] = 0;
     }
     for (int q = tid; q < TD_DIM; q += blockDim.x) d.sub_sp[(t & 1) * TD_DIM + q] = 0;
-    // thalamic gate of step t from the counts of step t-1 (thalamic_gate.cu:53-142)
     for (int col = tid; col < d.ncol; col += blockDim.x) {
         float4 g = d.gates[col];
-        float cur = s_prev_ok ? pm_i2f(d.col_sp[((t - 1) & 1) * d.ncol + col]) : 0.0f;
-        float l6c = s_prev_ok ? pm_i2f(d.l6_sp[((t - 1) & 1) * d.ncol + col]) : 0.0f;
-        float den = g.y > 1.0f ? g.y : 1.0f;
-        float an = fminf(1.0f, fmaxf(-1.0f, pm_div(pm_sub(g.y, cur), den)));
-        float l6d = g.w > 1.0f ? g.w : 1.0f;
-        float l6n = fminf(1.0f, fmaxf(-1.0f, pm_div(pm_sub(g.w, l6c), l6d)));
+        const float cur = prev_ok ? pm_i2f(d.col_sp[((t - 1) & 1) * d.ncol + col]) : 0.0f;
+        const float l6c = prev_ok ? pm_i2f(d.l6_sp[((t - 1) & 1) * d.ncol + col]) : 0.0f;
+        const float den = g.y > 1.0f ? g.y : 1.0f;
+        const float an = fminf(1.0f, fmaxf(-1.0f, pm_div(pm_sub(g.y, cur), den)));
+        const float l6d = g.w > 1.0f ? g.w : 1.0f;
+        const float l6n = fminf(1.0f, fmaxf(-1.0f, pm_div(pm_sub(g.w, l6c), l6d)));
         float nov = 0.0f;
         if (s_inject) {
-            unsigned tm = s_total_h > 1u ? s_total_h : 1u;
+            const unsigned tm = s_total_h > 1u ? s_total_h : 1u;
             nov = pm_sub(1.0f, pm_div(pm_u2f(s_bc), pm_u2f(tm)));
             nov = fminf(1.0f, fmaxf(0.0f, nov));
         }
@@ -282,11 +232,79 @@ __global__ void __launch_bounds__(256) k_control(Dev d, Consts k) {
         d.gates[col] = g;
     }
     __syncthreads();
-    if (tid == 0 && s_inject) d.byte_hist_nov[s_byte] += (unsigned)d.ncol;
+    if (tid == 0 && s_inject) {
+        d.byte_hist_nov[s_byte] += (unsigned)d.ncol;
+        c->hist_total += (unsigned)d.ncol;
+    }
 }
 
 // ---------------------------------------------------------------------------
-// k_neurons: one thread per neuron.
+// end of step t: the host-side work the reference does after the dispatch of
+// step t (src/stage2e/scheduler.cu:576-670): inhibition drive / kWTA size for
+// step t+1 (:688-722), modulators + TD value function (:724-751,
+// modulatory_kernels.cu:176-254), statistics.  Runs in one thread at the
+// start of k_synapses (all of step t's neuron counters are final by then).
+// ---------------------------------------------------------------------------
+__device__ void step_epilogue(const Dev& d, const Consts& k) {
+    Ctrl* c = d.ctrl;
+    const long long t = c->t;
+    const int sp = c->step_spikes[t & 1];
+    const float avg = c->total_steps > 0
+                          ? pm_div(pm_ll2f(c->total_spikes), pm_ll2f(c->total_steps))
+                          : 0.0f;
+    c->inh_active = 0;
+    if (t % 10 == 0) {
+        float drive = pm_div(pm_i2f(c->last_spikes), pm_add(avg, 1.0f));
+        drive = clampf(drive, 0.0f, 2.0f);
+        c->gdrive = pm_mul(drive, 0.15f);
+        const int kk = (int)pm_mul(pm_div(avg, pm_i2f(d.ncol)), 0.5f);
+        c->kwta_k = kk < 3 ? 3 : (kk > 5 ? 5 : kk);
+        c->inh_active = 1;
+    }
+    if (t % 100 == 0 && !c->e0) {
+        const float cur = pm_i2f(c->last_spikes);
+        float nov = avg > 0.0f ? pm_div(fabsf(pm_sub(cur, avg)), pm_add(avg, 1.0f)) : 0.0f;
+        if (nov > 1.0f) nov = 1.0f;
+        const float pred = (cur > 10.0f && cur < 1000.0f) ? 0.5f : 0.1f;
+        const float reward = pm_add(pm_mul(0.5f, nov), pm_mul(0.3f, pred));
+        const int* sub = d.sub_sp + (t & 1) * TD_DIM;
+        const float per = pm_i2f(d.per_sub);
+        float vs = 0.0f;
+        for (int q = 0; q < TD_DIM; ++q) vs = pm_fma(d.w_value[q], pm_div(pm_i2f(sub[q]), per), vs);
+        const float om = pm_sub(1.0f, 0.99f);
+        float vsp = 0.0f;
+        for (int q = 0; q < TD_DIM; ++q) {
+            const float f = pm_div(pm_i2f(sub[q]), per);
+            d.baseline[q] = pm_fma(0.99f, d.baseline[q], pm_mul(om, f));
+            vsp = pm_fma(d.w_value[q], pm_mul(d.w_pred[q], f), vsp);
+        }
+        const float delta = pm_sub(pm_add(reward, pm_mul(0.9f, vsp)), vs);
+        for (int q = 0; q < TD_DIM; ++q) {
+            const float f = pm_div(pm_i2f(sub[q]), per);
+            d.w_value[q] = clampf(pm_fma(pm_mul(0.001f, delta), f, d.w_value[q]), -1.0f, 1.0f);
+            const float pe = pm_sub(f, d.baseline[q]);
+            d.w_pred[q] = pm_fma(pm_mul(0.001f, pe), f, d.w_pred[q]);
+        }
+        float sig[4];
+        sig[0] = pm_add(0.1f, delta > 0.0f ? delta : pm_mul(0.3f, delta));
+        if (sig[0] < 0.0f) sig[0] = 0.0f;
+        sig[1] = pm_add(pm_add(0.2f, pm_mul(0.3f, nov)), pm_mul(0.1f, pred));
+        sig[2] = 0.05f;
+        sig[3] = 0.1f;
+        if (delta < -0.5f) sig[3] = pm_add(sig[3], pm_mul(0.3f, fabsf(delta)));
+        for (int m = 0; m < 4; ++m)
+            c->conc[m] = clampf(pm_fma(c->conc[m], k.mod_dec[m], sig[m]), 0.0f, 2.0f);
+    }
+    c->total_steps += 1;
+    c->total_spikes += sp;
+    if (t % k.inject_interval == 0) c->inject_spikes += sp;
+    c->last_spikes = sp;
+    const unsigned long long arr = c->step_arrivals[t & 1];
+    if (arr > 750000ull) c->dropped_ref += arr - 750000ull;
+}
+
+// ---------------------------------------------------------------------------
+// k_neurons: one thread per neuron, then the CTA's outgoing synapse groups.
 //   input .......... input_encoding.cu:117-164 (hashes recomputed per L4 neuron,
 //                    duplicates added in hash order)
 //   inhibition ..... scheduler.cu:112-133 + 234-265 (computed at step t from
@@ -295,21 +313,21 @@ __global__ void __launch_bounds__(256) k_control(Dev d, Consts k) {
 //   AdEx ........... neuron_kernels.cu:61-165
 //   groups ......... synapse_kernels.cu:123-141 (arrival conductance), :84-94
 //                    (decays, FF recovery), :176-194 / :282 (pre trace),
-//                    :334-387 (STP)
+//                    :334-387 (STP); one thread per group of the CTA's neurons
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) k_neurons(Dev d, Consts k) {
+__global__ void __launch_bounds__(NEU_BLOCK) k_neurons(Dev d, Consts k) {
+    __shared__ unsigned s_hist[NEU_BLOCK];
     const Ctrl* c = d.ctrl;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     const long long t = c->t;
     const bool valid = i < d.N;
     unsigned spike = 0;
-    int col = -1;
+    unsigned hist = 0;
     if (valid) {
         const unsigned info = d.info[i];
         const int type = info & 1, region = (info >> 1) & 7, subtype = (info >> 4) & 3;
-        col = (region != PF) ? (int)(info >> 8) : -1;
+        const int col = (region != PF) ? (int)(info >> 8) : -1;
         float input = d.input[i];
-        // population-coded byte input into L4 (k is the hash order)
         if (c->inject && region == L4) {
             const int off = i - col * d.NPC;
             const int b = c->byte;
@@ -322,11 +340,10 @@ __global__ void __launch_bounds__(256) k_neurons(Dev d, Consts k) {
                 if ((int)(h % (unsigned)d.l4) == off) input = pm_add(input, v);
             }
         }
-        // inhibition (set after step t-1 when (t-1) % 10 == 0, cleared otherwise)
         float inh = 0.0f;
         if (c->inh_active) {
-            float sg = subtype == 0 ? 1.40f : subtype == 1 ? 0.85f : subtype == 2 ? 1.10f : 1.0f;
-            float rg = region == PF ? 0.60f : 1.0f;
+            const float sg = subtype == 0 ? 1.40f : subtype == 1 ? 0.85f : subtype == 2 ? 1.10f : 1.0f;
+            const float rg = region == PF ? 0.60f : 1.0f;
             float cur = pm_mul(pm_mul(pm_fma(d.fr[i], 2.0f, c->gdrive), sg), rg);
             if (type == 1) cur = pm_mul(cur, 0.35f);
             if (cur > 2.0f) cur = 2.0f;
@@ -344,30 +361,27 @@ __global__ void __launch_bounds__(256) k_neurons(Dev d, Consts k) {
                 }
             }
         }
-        // AdEx
         int ref = d.ref[i];
         float fr = d.fr[i];
         float V = d.V[i];
         unsigned short off = d.off[i];
         if (ref > 0) {
-            ref -= 1;
-            fr = pm_mul(fr, k.fr_refr);
-            d.ref[i] = ref;
-            d.fr[i] = fr;
+            d.ref[i] = ref - 1;
+            d.fr[i] = pm_mul(fr, k.fr_refr);
         } else {
-            float s = pm_fma(d.s[i], k.syn_keep, pm_mul(input, k.syn_in));
-            float I = pm_sub(pm_add(s, d.nmda_cur[i]), inh);
+            const float s = pm_fma(d.s[i], k.syn_keep, pm_mul(input, k.syn_in));
+            const float I = pm_sub(pm_add(s, d.nmda_cur[i]), inh);
             float w = d.wad[i];
             float ea = pm_div(pm_sub(V, k.vt), k.dT);
             if (ea > 10.0f) ea = 10.0f;
             if (ea < -10.0f) ea = -10.0f;
-            float et = pm_mul(k.dT, snn_expf(ea));
-            float dV = pm_mul(pm_add(pm_sub(pm_add(-V, et), w), I), k.inv_taum);
-            float dw = pm_mul(pm_fma(k.a_ad, V, -w), k.inv_tauw);
+            const float et = pm_mul(k.dT, snn_expf(ea));
+            const float dV = pm_mul(pm_add(pm_sub(pm_add(-V, et), w), I), k.inv_taum);
+            const float dw = pm_mul(pm_fma(k.a_ad, V, -w), k.inv_tauw);
             V = pm_add(V, dV);
             w = pm_add(w, dw);
             V = clampf(V, k.vmin, k.vmax);
-            float theta = pm_add(1.0f, pm_div(pm_u2f(off), 256.0f));
+            const float theta = pm_add(1.0f, pm_div(pm_u2f(off), 256.0f));
             float can = d.can[i];
             if (V >= theta) {
                 spike = 1;
@@ -402,9 +416,8 @@ __global__ void __launch_bounds__(256) k_neurons(Dev d, Consts k) {
         float xp = pm_mul(d.xpost[i], k.dec_xpost);
         if (spike) xp = pm_add(xp, k.a_minus);
         d.xpost[i] = xp;
-        const unsigned hist = (d.hist[i] << 1) | spike;
+        hist = (d.hist[i] << 1) | spike;
         d.hist[i] = hist;
-        // counters of this step
         if (spike) {
             atomicAdd(&d.ctrl->step_spikes[t & 1], 1);
             if (i / d.per_sub < TD_DIM) atomicAdd(&d.sub_sp[(t & 1) * TD_DIM + i / d.per_sub], 1);
@@ -418,50 +431,71 @@ __global__ void __launch_bounds__(256) k_neurons(Dev d, Consts k) {
             }
             atomicAdd(&d.ctrl->ltp_visits, (unsigned long long)(d.in_ptr[i + 1] - d.in_ptr[i]));
         }
-        // outgoing synapse groups of neuron i
-        unsigned long long arr_cnt = 0, disp_cnt = 0;
-        const int g0 = d.gbeg[i], g1 = d.gbeg[i + 1];
-        for (int g = g0; g < g1; ++g) {
-            const unsigned meta = d.gmeta[g];
-            const int dd = meta & GV_D_MASK;
-            const bool ff = meta & GV_FF, exc = meta & GV_EXC;
-            const bool arr = (hist >> dd) & 1u;
-            const bool nxt = (hist >> (dd - 1)) & 1u;
-            float4 st = d.gstate[g];  // R, u, nmda, xpre
-            if (arr && exc) st.z = pm_fma(pm_mul(k.g_nmda, st.x), st.y, st.z);
-            st.z = pm_mul(st.z, k.dec_nmda);
-            if (ff) st.x = pm_fma(pm_sub(1.0f, st.x), k.rec_ff_step, st.x);
-            st.w = pm_mul(st.w, k.dec_xpre);
-            const float x_ltp = st.w;
-            if (arr) {
-                st.w = pm_add(st.w, k.a_plus);
-                const int cl = ff ? 0 : (exc ? 1 : 2);
-                const float U = k.U[cl];
-                st.x = pm_fma(pm_sub(1.0f, st.x), k.rec[cl], st.x);
-                st.y = pm_fma(pm_sub(st.y, U), k.fac[cl], U);
-                const float un = pm_fma(U, pm_sub(1.0f, st.y), st.y);
-                const float rn = pm_mul(st.x, pm_sub(1.0f, un));
-                st.y = un > 1.0f ? 1.0f : un;
-                st.x = rn < 0.0f ? 0.0f : rn;
-                arr_cnt += (unsigned long long)d.gsize[g];
-            }
-            if (spike) disp_cnt += (unsigned long long)d.gsize[g];
-            d.gstate[g] = st;
-            const unsigned fl = (meta & (GV_D_MASK | GV_FF | GV_EXC)) | (arr ? GV_ARR : 0u) |
-                                (nxt ? GV_NEXT : 0u) | (spike ? GV_DISP : 0u);
-            d.gview[g] = make_float4(st.z, x_ltp, st.x, __uint_as_float(fl));
+    }
+    s_hist[threadIdx.x] = hist;
+    const unsigned word = __ballot_sync(0xffffffffu, spike != 0);
+    if ((threadIdx.x & 31) == 0 && (i >> 5) < d.words) {
+        const long long row = (t - c->raster_base) % d.raster_cap;
+        d.raster[row * d.words + (i >> 5)] = word;
+    }
+    __syncthreads();
+    // outgoing synapse groups of this CTA's neurons, one thread per group
+    const int i0 = blockIdx.x * blockDim.x;
+    const int i1 = min(i0 + (int)blockDim.x, d.N);
+    const int g0 = d.gbeg[i0], g1 = d.gbeg[i1];
+    unsigned long long arr_cnt = 0, disp_cnt = 0;
+    auto group_update = [&](int g, unsigned meta, float4 st) {
+        const unsigned h = s_hist[gw_lpre(meta)];
+        const int dd = meta & GV_D_MASK;
+        const bool ff = meta & GV_FF, exc = meta & GV_EXC;
+        const bool arr = (h >> dd) & 1u;
+        const bool nxt = (h >> (dd - 1)) & 1u;
+        const bool disp = h & 1u;
+        if (arr && exc) st.z = pm_fma(pm_mul(k.g_nmda, st.x), st.y, st.z);
+        st.z = pm_mul(st.z, k.dec_nmda);
+        if (ff) st.x = pm_fma(pm_sub(1.0f, st.x), k.rec_ff_step, st.x);
+        st.w = pm_mul(st.w, k.dec_xpre);
+        const float x_ltp = st.w;
+        if (arr) {
+            st.w = pm_add(st.w, k.a_plus);
+            const int cl = ff ? 0 : (exc ? 1 : 2);
+            const float U = k.U[cl];
+            st.x = pm_fma(pm_sub(1.0f, st.x), k.rec[cl], st.x);
+            st.y = pm_fma(pm_sub(st.y, U), k.fac[cl], U);
+            const float un = pm_fma(U, pm_sub(1.0f, st.y), st.y);
+            const float rn = pm_mul(st.x, pm_sub(1.0f, un));
+            st.y = un > 1.0f ? 1.0f : un;
+            st.x = rn < 0.0f ? 0.0f : rn;
+            arr_cnt += gw_size(meta);
         }
+        if (disp) disp_cnt += gw_size(meta);
+        d.gstate[g] = st;
+        const unsigned fl = (meta & (GV_D_MASK | GV_FF | GV_EXC)) | (arr ? GV_ARR : 0u) |
+                            (nxt ? GV_NEXT : 0u) | (disp ? GV_DISP : 0u);
+        d.gview[g] = make_float4(st.z, x_ltp, st.x, __uint_as_float(fl));
+    };
+    // two groups per iteration keep independent loads in flight
+    const int stride = 2 * blockDim.x;
+    for (int g = g0 + (int)threadIdx.x; g < g1; g += stride) {
+        const int g2 = g + blockDim.x;
+        const unsigned m0 = d.gmeta[g];
+        const unsigned m1 = g2 < g1 ? d.gmeta[g2] : 0u;
+        const float4 s0 = d.gstate[g];
+        const float4 s1 = g2 < g1 ? d.gstate[g2] : make_float4(0, 0, 0, 0);
+        group_update(g, m0, s0);
+        if (g2 < g1) group_update(g2, m1, s1);
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+        arr_cnt += __shfl_xor_sync(0xffffffffu, arr_cnt, o);
+        disp_cnt += __shfl_xor_sync(0xffffffffu, disp_cnt, o);
+    }
+    if ((threadIdx.x & 31) == 0) {
         if (arr_cnt) {
             atomicAdd(&d.ctrl->arrivals, arr_cnt);
             atomicAdd(&d.ctrl->step_arrivals[t & 1], arr_cnt);
         }
         if (disp_cnt) atomicAdd(&d.ctrl->dispatched, disp_cnt);
-    }
-    // spike raster word of this warp
-    const unsigned word = __ballot_sync(0xffffffffu, spike != 0);
-    if ((threadIdx.x & 31) == 0 && (i >> 5) < d.words) {
-        const long long row = (t - c->raster_base) % d.raster_cap;
-        d.raster[row * d.words + (i >> 5)] = word;
     }
 }
 
@@ -476,124 +510,249 @@ __global__ void __launch_bounds__(256) k_neurons(Dev d, Consts k) {
 //   PSW decay ....... scheduler.cu:55-86 (every 1000 steps)
 // Both sums use the canonical order: 32-synapse chunks in ascending
 // reference synapse id, xor butterfly inside a chunk, chunks added in order.
+// Each lane carries two chunks at once (independent loads in flight).
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) k_synapses(Dev d, Consts k) {
-    const int lane = threadIdx.x & 31;
-    const int j = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    if (j >= d.N) return;
-    const Ctrl* c = d.ctrl;
-    const long long t = c->t;
-    const float gain = c->gain;
-    const bool e0 = c->e0 != 0;
-    const bool do10 = (t % 10 == 0) && !e0;
-    const bool do1000 = (t % 1000 == 0);
-    const float prune = c->prune_thr;
-    const float Vj = d.V[j];
-    const float mgj = d.mg[j];
-    const bool post_spk = d.hist[j] & 1u;
-    const float xpost = d.xpost[j];
-    const float one_m_V = pm_sub(k.e_rev, Vj);
-    const int slot_now = (int)((t / 3) & (VAL_SLOTS - 1));
-    const int b = d.in_ptr[j], e = d.in_ptr[j + 1];
-    float acc_nmda = 0.0f, acc_in = 0.0f;
-    for (int base = b; base < e; base += 32) {
-        const int p = base + lane;
-        float term_nmda = 0.0f, term_in = 0.0f;
-        if (p < e) {
-            const unsigned g = d.gid[p];
-            const float4 v = d.gview[g];
-            const unsigned fl = __float_as_uint(v.w);
-            const bool ff = fl & GV_FF, exc = fl & GV_EXC;
-            const int dd = fl & GV_D_MASK;
-            float ca = 0.0f;
-            if (exc) {
-                ca = d.ca[p];
-                ca = pm_mul(ca, ff ? k.dec_ca_ff : k.dec_ca);
-                const float nm = pm_mul(v.x, mgj);
-                ca = pm_fma(nm, k.ca_gain, ca);
-                const float cmax = ff ? k.ca_max_ff : k.ca_max;
-                if (ca > cmax) ca = cmax;
-                d.ca[p] = ca;
-                const float I = pm_mul(pm_mul(nm, one_m_V), k.i_gain);
-                if (fabsf(I) > k.i_min) term_nmda = I;
-            }
-            const bool arr = fl & GV_ARR, disp = fl & GV_DISP, nxt = fl & GV_NEXT;
-            const bool touch = post_spk || arr || disp || do10 || do1000;
-            if (nxt && dd >= 2) {
-                const int sl = (int)(((t + 1 - dd) / 3) & (VAL_SLOTS - 1));
-                term_in = d.val[(long long)p * VAL_SLOTS + sl];
-            }
-            if (touch) {
-                float4 q = d.ev[p];  // alpha, beta, auto, elig
-                bool dirty = false;
-                const float eta = ff ? k.eta_ff : k.eta;
-                const float M = e0 ? 1.0f : c->M[exc ? 1 : 0];  // [0] inhibitory, [1] excitatory pre
-                const float pf = e0 ? 1.0f : pm_sub(1.0f, pm_mul(0.5f, q.z));
-                if (post_spk) {  // LTP from the pre trace (dense pass, post spiked)
-                    const float dw = pm_fma(v.y, k.a_plus, 0.0f);
-                    if (dw > 0.0f) q.x = pm_fma(pm_mul(pm_mul(pm_mul(eta, dw), gain), M), pf, q.x);
-                    if (ca > k.reb_thr) {
-                        const float ex = pm_sub(ca, k.reb_thr);
-                        q.y = pm_fma(pm_mul(pm_mul(pm_mul(eta, ex), k.reb_gain), gain), M, q.y);
-                    }
-                    q.w = pm_add(q.w, dw);
-                    dirty = true;
-                }
-                if (arr) {  // LTD at arrival from the post trace
-                    const float dw = pm_mul(-xpost, k.a_minus);
-                    if (dw < 0.0f) q.y = pm_fma(pm_mul(pm_mul(pm_mul(eta, -dw), gain), M), pf, q.y);
-                    q.w = pm_add(q.w, dw);
-                    dirty = true;
-                }
-                if (disp) {  // value this dispatch delivers d steps later
-                    const float wm = pm_div(pm_mul(k.w_max, q.x), pm_add(q.x, q.y));
-                    const float val = pm_mul(exc ? wm : -wm, v.z);
-                    if (dd == 1) term_in = val;
-                    else d.val[(long long)p * VAL_SLOTS + slot_now] = val;
-                }
-                if (do10) {
-                    if (exc) {
-                        float act = d.act[p], au = q.z;
-                        const float ca4 = pm_mul(pm_mul(pm_mul(ca, ca), ca), ca);
-                        const float da = pm_fma(pm_mul(k.ck_k1, ca4), pm_sub(1.0f, act),
-                                                -pm_mul(pm_mul(k.ck_k2, act), k.ck_pp1));
-                        const float du = pm_fma(pm_mul(pm_mul(k.ck_k3, act), act), pm_sub(1.0f, au),
-                                                -pm_mul(pm_mul(k.ck_k4, au), k.ck_pp1));
-                        act = clampf(pm_fma(da, k.ck_dt, act), 0.0f, 1.0f);
-                        au = clampf(pm_fma(du, k.ck_dt, au), 0.0f, 1.0f);
-                        d.act[p] = act;
-                        q.z = au;
-                    }
-                    const float a1 = pm_fma(d.e1[p], k.e1_dec, q.w);
-                    const float a2 = pm_fma(d.e2[p], k.e2_dec, a1);
-                    d.e1[p] = a1;
-                    d.e2[p] = a2;
-                    q.w = 0.0f;
-                    dirty = true;
-                }
-                if (do1000) {
-                    float a = pm_mul(q.x, k.psw_decay), bb = pm_mul(q.y, k.psw_decay);
-                    if (a < k.ab_min) a = k.ab_min;
-                    if (bb < k.ab_min) bb = k.ab_min;
-                    if (pm_add(a, bb) < prune) { a = k.ab_reset; bb = k.ab_reset; }
-                    q.x = a;
-                    q.y = bb;
-                    dirty = true;
-                }
-                if (dirty) d.ev[p] = q;
-            }
-        }
-#pragma unroll
-        for (int o = 16; o >= 1; o >>= 1) {
-            term_nmda = pm_add(term_nmda, __shfl_xor_sync(0xffffffffu, term_nmda, o));
-            term_in = pm_add(term_in, __shfl_xor_sync(0xffffffffu, term_in, o));
-        }
-        acc_nmda = pm_add(acc_nmda, term_nmda);
-        acc_in = pm_add(acc_in, term_in);
+struct PostCtx {
+    long long t;
+    float gain, prune, Mexc, Minh, Vj, mgj, xpost, one_m_V;
+    bool post_spk, e0, do10, do1000;
+    int slot_now;
+};
+
+__device__ __forceinline__ void synapse_one(const Dev& d, const Consts& k, const PostCtx& pc,
+                                            int p, unsigned gw, float4 v, float ca_in,
+                                            float& term_nmda, float& term_in) {
+    const unsigned fl = __float_as_uint(v.w);
+    const bool ff = gw & (1u << 30), exc = gw >> 31;
+    const int dd = fl & GV_D_MASK;
+    float ca = 0.0f;
+    if (exc) {
+        ca = pm_mul(ca_in, ff ? k.dec_ca_ff : k.dec_ca);
+        const float nm = pm_mul(v.x, pc.mgj);
+        ca = pm_fma(nm, k.ca_gain, ca);
+        const float cmax = ff ? k.ca_max_ff : k.ca_max;
+        if (ca > cmax) ca = cmax;
+        d.ca[p] = ca;
+        const float I = pm_mul(pm_mul(nm, pc.one_m_V), k.i_gain);
+        if (fabsf(I) > k.i_min) term_nmda = I;
     }
-    if (lane == 0) {
-        d.nmda_cur[j] = acc_nmda;
-        d.input[j] = acc_in;
+    const bool arr = fl & GV_ARR, disp = fl & GV_DISP, nxt = fl & GV_NEXT;
+    if (nxt && dd >= 2) {
+        const int sl = (int)(((pc.t + 1 - dd) / 3) & (VAL_SLOTS - 1));
+        term_in = d.val[(long long)p * VAL_SLOTS + sl];
+    }
+    if (pc.post_spk || arr || disp || pc.do10 || pc.do1000) {
+        float4 q = d.ev[p];  // alpha, beta, auto, elig
+        bool dirty = false;
+        const float eta = ff ? k.eta_ff : k.eta;
+        const float M = pc.e0 ? 1.0f : (exc ? pc.Mexc : pc.Minh);
+        const float pf = pc.e0 ? 1.0f : pm_sub(1.0f, pm_mul(0.5f, q.z));
+        if (pc.post_spk) {  // LTP from the pre trace (post spiked)
+            const float dw = pm_fma(v.y, k.a_plus, 0.0f);
+            if (dw > 0.0f) q.x = pm_fma(pm_mul(pm_mul(pm_mul(eta, dw), pc.gain), M), pf, q.x);
+            if (ca > k.reb_thr) {
+                const float ex = pm_sub(ca, k.reb_thr);
+                q.y = pm_fma(pm_mul(pm_mul(pm_mul(eta, ex), k.reb_gain), pc.gain), M, q.y);
+            }
+            q.w = pm_add(q.w, dw);
+            dirty = true;
+        }
+        if (arr) {  // LTD at arrival from the post trace
+            const float dw = pm_mul(-pc.xpost, k.a_minus);
+            if (dw < 0.0f) q.y = pm_fma(pm_mul(pm_mul(pm_mul(eta, -dw), pc.gain), M), pf, q.y);
+            q.w = pm_add(q.w, dw);
+            dirty = true;
+        }
+        if (disp) {  // value this dispatch delivers d steps later
+            const float wm = pm_div(pm_mul(k.w_max, q.x), pm_add(q.x, q.y));
+            const float val = pm_mul(exc ? wm : -wm, v.z);
+            if (dd == 1) term_in = val;
+            else d.val[(long long)p * VAL_SLOTS + pc.slot_now] = val;
+        }
+        if (pc.do10) {
+            if (exc) {
+                float act = d.act[p], au = q.z;
+                const float ca4 = pm_mul(pm_mul(pm_mul(ca, ca), ca), ca);
+                const float da = pm_fma(pm_mul(k.ck_k1, ca4), pm_sub(1.0f, act),
+                                        -pm_mul(pm_mul(k.ck_k2, act), k.ck_pp1));
+                const float du = pm_fma(pm_mul(pm_mul(k.ck_k3, act), act), pm_sub(1.0f, au),
+                                        -pm_mul(pm_mul(k.ck_k4, au), k.ck_pp1));
+                act = clampf(pm_fma(da, k.ck_dt, act), 0.0f, 1.0f);
+                au = clampf(pm_fma(du, k.ck_dt, au), 0.0f, 1.0f);
+                d.act[p] = act;
+                q.z = au;
+            }
+            const float a1 = pm_fma(d.e1[p], k.e1_dec, q.w);
+            const float a2 = pm_fma(d.e2[p], k.e2_dec, a1);
+            d.e1[p] = a1;
+            d.e2[p] = a2;
+            q.w = 0.0f;
+            dirty = true;
+        }
+        if (pc.do1000) {
+            float a = pm_mul(q.x, k.psw_decay), bb = pm_mul(q.y, k.psw_decay);
+            if (a < k.ab_min) a = k.ab_min;
+            if (bb < k.ab_min) bb = k.ab_min;
+            if (pm_add(a, bb) < pc.prune) { a = k.ab_reset; bb = k.ab_reset; }
+            q.x = a;
+            q.y = bb;
+            dirty = true;
+        }
+        if (dirty) d.ev[p] = q;
+    }
+}
+
+// --- bulk async copy (1D TMA) helpers -------------------------------------
+__device__ __forceinline__ unsigned smem_u32(const void* p) {
+    return static_cast<unsigned>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(unsigned long long* bar, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(unsigned long long* bar, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+// global -> shared bulk copy completing on `bar` (16-byte aligned, size % 16 == 0)
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes,
+                                         unsigned long long* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, unsigned parity) {
+    unsigned ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+constexpr int SYN_THREADS = 512;       // 16 warps per CTA
+constexpr int SYN_WARPS = SYN_THREADS / 32;
+constexpr unsigned WAIT_LIMIT = 1u << 24;  // bounded spin (~seconds) before flagging an error
+
+// one tile = consecutive post-synaptic neurons [tile_post[k], tile_post[k+1])
+// whose incoming synapses [in_ptr[j0], in_ptr[j1]) fit the staging buffers
+__device__ __forceinline__ void tile_range(const Dev& d, int tile, int& j0, int& j1, int& a0,
+                                           int& a1) {
+    j0 = d.tile_post[tile];
+    j1 = d.tile_post[tile + 1];
+    a0 = d.in_ptr[j0] & ~3;
+    a1 = (d.in_ptr[j1] + 3) & ~3;
+}
+
+__global__ void __launch_bounds__(SYN_THREADS) k_synapses(Dev d, Consts k) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    __shared__ __align__(8) unsigned long long bars[2];
+    unsigned* const sbase = reinterpret_cast<unsigned*>(smem_raw);
+    const int cap = d.tile_cap;  // stage s: gid at sbase + 2*cap*s, ca right after it
+    if (blockIdx.x == 0 && threadIdx.x == 0) step_epilogue(d, k);
+    if (threadIdx.x == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    const Ctrl* c = d.ctrl;
+    PostCtx pc;
+    pc.t = c->t;
+    pc.gain = c->gain;
+    pc.prune = c->prune_thr;
+    pc.Mexc = c->M[1];
+    pc.Minh = c->M[0];
+    pc.e0 = c->e0 != 0;
+    pc.do10 = (pc.t % 10 == 0) && !pc.e0;
+    pc.do1000 = (pc.t % 1000 == 0);
+    pc.slot_now = (int)((pc.t / 3) & (VAL_SLOTS - 1));
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    // thread 0 only: stage the gid / ca streams of `tile` into buffer `stage`
+    auto issue = [&](int tile, int stage) {
+        int j0, j1, a0, a1;
+        tile_range(d, tile, j0, j1, a0, a1);
+        const unsigned bytes = (unsigned)(a1 - a0) * 4u;
+        unsigned* dst = sbase + 2 * cap * stage;
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_expect_tx(&bars[stage], 2u * bytes);
+        if (bytes > 0) {
+            bulk_g2s(dst, d.gid + a0, bytes, &bars[stage]);
+            bulk_g2s(dst + cap, d.ca + a0, bytes, &bars[stage]);
+        }
+    };
+    unsigned phases = 0u;  // bit s = parity of the next wait on stage s
+    int it = 0;
+    if (threadIdx.x == 0 && (int)blockIdx.x < d.n_tiles) issue(blockIdx.x, 0);
+    for (int tile = blockIdx.x; tile < d.n_tiles; tile += gridDim.x, ++it) {
+        const int stage = it & 1;
+        const int next = tile + gridDim.x;
+        if (threadIdx.x == 0 && next < d.n_tiles) issue(next, stage ^ 1);
+        // wait for this tile's streams (bounded)
+        bool ok = false;
+        for (unsigned spin = 0; spin < WAIT_LIMIT; ++spin) {
+            if (mbar_try_wait(&bars[stage], (phases >> stage) & 1u)) { ok = true; break; }
+        }
+        phases ^= 1u << stage;
+        if (__syncthreads_or(!ok)) {
+            if (threadIdx.x == 0) {
+                atomicOr(&d.ctrl->error, 1);
+                // drain the copy already issued for the next tile (bounded) before exiting
+                if (next < d.n_tiles)
+                    for (unsigned spin = 0; spin < WAIT_LIMIT; ++spin)
+                        if (mbar_try_wait(&bars[stage ^ 1], (phases >> (stage ^ 1)) & 1u)) break;
+            }
+            return;
+        }
+        int j0, j1, a0, a1;
+        tile_range(d, tile, j0, j1, a0, a1);
+        const unsigned* sg = sbase + 2 * cap * stage;
+        const float* sc = reinterpret_cast<const float*>(sg + cap);
+        for (int j = j0 + warp; j < j1; j += SYN_WARPS) {
+            pc.Vj = d.V[j];
+            pc.mgj = d.mg[j];
+            pc.post_spk = d.hist[j] & 1u;
+            pc.xpost = d.xpost[j];
+            pc.one_m_V = pm_sub(k.e_rev, pc.Vj);
+            const int b = d.in_ptr[j], e = d.in_ptr[j + 1];
+            float acc_nmda = 0.0f, acc_in = 0.0f;
+            for (int base = b; base < e; base += 64) {
+                const int p0 = base + lane, p1 = base + 32 + lane;
+                const bool v0 = p0 < e, v1 = p1 < e;
+                const unsigned gw0 = v0 ? sg[p0 - a0] : 0u;
+                const unsigned gw1 = v1 ? sg[p1 - a0] : 0u;
+                const float ca0 = v0 ? sc[p0 - a0] : 0.0f;
+                const float ca1 = v1 ? sc[p1 - a0] : 0.0f;
+                const float4 w0 = v0 ? d.gview[gw0 & 0x3fffffffu] : make_float4(0, 0, 0, 0);
+                const float4 w1 = v1 ? d.gview[gw1 & 0x3fffffffu] : make_float4(0, 0, 0, 0);
+                float n0 = 0.0f, i0 = 0.0f, n1 = 0.0f, i1 = 0.0f;
+                if (v0) synapse_one(d, k, pc, p0, gw0, w0, ca0, n0, i0);
+                if (v1) synapse_one(d, k, pc, p1, gw1, w1, ca1, n1, i1);
+#pragma unroll
+                for (int o = 16; o >= 1; o >>= 1) {
+                    n0 = pm_add(n0, __shfl_xor_sync(0xffffffffu, n0, o));
+                    i0 = pm_add(i0, __shfl_xor_sync(0xffffffffu, i0, o));
+                    n1 = pm_add(n1, __shfl_xor_sync(0xffffffffu, n1, o));
+                    i1 = pm_add(i1, __shfl_xor_sync(0xffffffffu, i1, o));
+                }
+                acc_nmda = pm_add(acc_nmda, n0);
+                acc_in = pm_add(acc_in, i0);
+                if (base + 32 < e) {
+                    acc_nmda = pm_add(acc_nmda, n1);
+                    acc_in = pm_add(acc_in, i1);
+                }
+            }
+            if (lane == 0) {
+                d.nmda_cur[j] = acc_nmda;
+                d.input[j] = acc_in;
+            }
+        }
+        // every thread is done with this stage before it is refilled
+        __syncthreads();
     }
 }
 
@@ -610,6 +769,7 @@ struct Engine2e : snnb::Engine {
     bool built = false;
     long long steps = 0;
     int raster_cap = 1024;
+    long long raster_base_host = 0;  // first step of the current raster rows
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t graph_exec = nullptr;
     int graph_steps = 0;
@@ -619,7 +779,7 @@ struct Engine2e : snnb::Engine {
     snn_profile prof{};
     // device buffers
     snnb::DevBuf<float> V, wad, s, fr, can, xpost, mg, input, nmda_cur, ca, act, e1, e2, val;
-    snnb::DevBuf<int> last, ref, gbeg, in_ptr, gsize, col_sp, l6_sp, sub_sp, byte_histogram,
+    snnb::DevBuf<int> last, ref, gbeg, in_ptr, gsize, gpre, col_sp, l6_sp, sub_sp, byte_histogram,
         neuron_byte_counts;
     snnb::DevBuf<unsigned short> off;
     snnb::DevBuf<unsigned> info, hist, gmeta, gid, byte_hist_nov, raster;
@@ -628,6 +788,10 @@ struct Engine2e : snnb::Engine {
     snnb::DevBuf<Ctrl> ctrl;
     snnb::DevBuf<unsigned char> corpus;
     snnb::DevBuf<int> counts_tmp;
+    snnb::DevBuf<int> tile_post;
+    int n_tiles = 0, tile_cap = 0, syn_grid = 1;
+    size_t syn_smem = 0;
+    static constexpr int TILE_POSTS = 16;
 
     explicit Engine2e(const snn_config& c) : cfg(c) {
         if (cfg.raster_steps > 0) raster_cap = cfg.raster_steps;
@@ -719,16 +883,52 @@ struct Engine2e : snnb::Engine {
         in_ptr.upload(lay.in_ptr.data(), N + 1, stream);
         // groups
         gmeta.alloc(G); gsize.alloc(G); gstate.alloc(G); gview.alloc(G);
-        gmeta.upload(lay.gmeta.data(), G, stream);
+        {
+            std::vector<unsigned> packed(G);
+            for (int64_t g = 0; g < G; ++g) {
+                SNN_REQUIRE(lay.gsize[g] < 65536, SNN_ERR_ARG, "synapse group too large");
+                packed[g] = (lay.gmeta[g] & 0x7fu) | ((unsigned)lay.gsize[g] << 8) |
+                            ((unsigned)(lay.gpre[g] % NEU_BLOCK) << 24);
+            }
+            gmeta.upload(packed.data(), G, stream);
+        }
         gsize.upload(lay.gsize.data(), G, stream);
+        gpre.alloc(G);
+        gpre.upload(lay.gpre.data(), G, stream);
         std::vector<float4> h_gs(G);
         for (int64_t g = 0; g < G; ++g) h_gs[g] = make_float4(1.0f, lay.gu0[g], 0.0f, 0.0f);
         gstate.upload(h_gs.data(), G, stream);
         gview.zero(stream);
         // synapses, post-major
-        gid.alloc(S); ca.alloc(S); ev.alloc(S); act.alloc(S); e1.alloc(S); e2.alloc(S);
+        // gid / ca are streamed in 16-byte aligned tiles: pad by 4 elements
+        gid.alloc(S + 4); ca.alloc(S + 4); ev.alloc(S); act.alloc(S); e1.alloc(S); e2.alloc(S);
         val.alloc((size_t)S * VAL_SLOTS);
+        gid.zero(stream);
         gid.upload(lay.gid_pm.data(), S, stream);
+        // synapse-pass tiles: TILE_POSTS consecutive post neurons each
+        {
+            std::vector<int> tp;
+            int cap = 4;
+            for (int j0 = 0; j0 < N; j0 += TILE_POSTS) {
+                const int j1 = std::min(N, j0 + TILE_POSTS);
+                tp.push_back(j0);
+                const int a0 = lay.in_ptr[j0] & ~3, a1 = (lay.in_ptr[j1] + 3) & ~3;
+                cap = std::max(cap, a1 - a0);
+            }
+            tp.push_back(N);
+            n_tiles = (int)tp.size() - 1;
+            tile_cap = (cap + 3) & ~3;
+            tile_post.alloc(tp.size());
+            tile_post.upload(tp.data(), tp.size(), stream);
+            const size_t smem = (size_t)4 * tile_cap * sizeof(unsigned);
+            SNN_REQUIRE(smem <= 200 * 1024, SNN_ERR_ARG, "synapse tile exceeds shared memory");
+            SNN_CUDA(cudaFuncSetAttribute(k_synapses, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)smem));
+            int sms = 0;
+            SNN_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, cfg.device));
+            syn_grid = std::min(n_tiles, 2 * sms);
+            syn_smem = smem;
+        }
         {
             std::vector<float4> h_ev(S);
             for (int64_t p = 0; p < S; ++p) {
@@ -769,7 +969,8 @@ struct Engine2e : snnb::Engine {
         D.V = V.p; D.wad = wad.p; D.s = s.p; D.fr = fr.p; D.can = can.p; D.xpost = xpost.p; D.mg = mg.p;
         D.input = input.p; D.nmda_cur = nmda_cur.p; D.last = last.p; D.ref = ref.p; D.off = off.p;
         D.info = info.p; D.hist = hist.p; D.gbeg = gbeg.p; D.in_ptr = in_ptr.p;
-        D.gmeta = gmeta.p; D.gsize = gsize.p; D.gstate = gstate.p; D.gview = gview.p;
+        D.gmeta = gmeta.p; D.gsize = gsize.p; D.gpre = gpre.p; D.gstate = gstate.p; D.gview = gview.p;
+        D.tile_post = tile_post.p; D.n_tiles = n_tiles; D.tile_cap = tile_cap;
         D.gid = gid.p; D.ca = ca.p; D.ev = ev.p; D.act = act.p; D.e1 = e1.p; D.e2 = e2.p; D.val = val.p;
         D.ctrl = ctrl.p; D.gates = gates.p; D.col_sp = col_sp.p; D.l6_sp = l6_sp.p; D.sub_sp = sub_sp.p;
         D.byte_hist_nov = byte_hist_nov.p; D.byte_histogram = byte_histogram.p;
@@ -807,15 +1008,16 @@ struct Engine2e : snnb::Engine {
     // (inside a stream capture the records must be "external" so that they
     // become event-record nodes that time the graph's kernels)
     void launch_step(cudaStream_t st, cudaEvent_t* ev = nullptr, bool capturing = false) {
-        const int nb = (D.N + 255) / 256;
+        const int nb = (D.N + NEU_BLOCK - 1) / NEU_BLOCK;
         const long long warps = D.N;
         const unsigned fl = capturing ? cudaEventRecordExternal : cudaEventRecordDefault;
         if (ev) SNN_CUDA(cudaEventRecordWithFlags(ev[0], st, fl));
-        k_control<<<1, 256, 0, st>>>(D, K);
+        k_control<<<1, 64, 0, st>>>(D, K);
         if (ev) SNN_CUDA(cudaEventRecordWithFlags(ev[1], st, fl));
-        k_neurons<<<nb, 256, 0, st>>>(D, K);
+        k_neurons<<<nb, NEU_BLOCK, 0, st>>>(D, K);
         if (ev) SNN_CUDA(cudaEventRecordWithFlags(ev[2], st, fl));
-        k_synapses<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(D, K);
+        (void)warps;
+        k_synapses<<<syn_grid, SYN_THREADS, syn_smem, st>>>(D, K);
         if (ev) SNN_CUDA(cudaEventRecordWithFlags(ev[3], st, fl));
     }
 
@@ -881,6 +1083,7 @@ struct Engine2e : snnb::Engine {
         int lr = learn ? 1 : 0;
         set_ctrl_field(offsetof(Ctrl, learn), &lr, sizeof(int));
         long long rb = steps;
+        raster_base_host = rb;
         set_ctrl_field(offsetof(Ctrl, raster_base), &rb, sizeof(rb));
         if (byte_override >= 0) {
             SNN_REQUIRE(byte_override < 256, SNN_ERR_ARG, "byte out of range");
@@ -934,7 +1137,17 @@ struct Engine2e : snnb::Engine {
         SNN_CUDA(cudaGetLastError());
     }
 
-    void sync() override { SNN_CUDA(cudaStreamSynchronize(stream)); }
+    void check_device_error() {
+        int err = 0;
+        SNN_CUDA(cudaMemcpyAsync(&err, (char*)ctrl.p + offsetof(Ctrl, error), sizeof(int),
+                                 cudaMemcpyDeviceToHost, stream));
+        SNN_CUDA(cudaStreamSynchronize(stream));
+        SNN_REQUIRE(err == 0, SNN_ERR_CUDA, "a kernel's bounded wait for its staged data ran out");
+    }
+    void sync() override {
+        SNN_CUDA(cudaStreamSynchronize(stream));
+        check_device_error();
+    }
     int64_t steps_done() const override { return steps; }
 
     void counters(snn_counters* o) override {
@@ -942,14 +1155,13 @@ struct Engine2e : snnb::Engine {
         Ctrl h;
         SNN_CUDA(cudaMemcpyAsync(&h, ctrl.p, sizeof(Ctrl), cudaMemcpyDeviceToHost, stream));
         SNN_CUDA(cudaStreamSynchronize(stream));
+        SNN_REQUIRE(h.error == 0, SNN_ERR_CUDA, "a kernel's bounded wait for its staged data ran out");
         memset(o, 0, sizeof(*o));
         o->step = steps;
-        o->total_spikes = h.total_spikes + (steps > 0 ? h.step_spikes[(steps - 1) & 1] : 0);
+        o->total_spikes = h.total_spikes;
         o->arrivals = (int64_t)h.arrivals;
         o->dispatched = (int64_t)h.dispatched;
         o->dropped_ref = (int64_t)h.dropped_ref;
-        if (steps > 0 && h.step_arrivals[(steps - 1) & 1] > 750000ull)
-            o->dropped_ref += (int64_t)(h.step_arrivals[(steps - 1) & 1] - 750000ull);
         o->ltp_visits = (int64_t)h.ltp_visits;
         o->burst_spikes = (int64_t)h.burst;
         o->n_neurons = net.N;
@@ -980,7 +1192,7 @@ struct Engine2e : snnb::Engine {
     void get_spikes(uint32_t* words, int64_t n_words) override {
         SNN_REQUIRE(built && steps > 0, SNN_ERR_STATE, "no step executed yet");
         SNN_REQUIRE(n_words >= D.words, SNN_ERR_ARG, "bitmask buffer too small");
-        const long long row = (steps - 1) % raster_cap;
+        const long long row = (steps - 1 - raster_base_host) % raster_cap;
         SNN_CUDA(cudaMemcpyAsync(words, raster.p + row * D.words, D.words * sizeof(unsigned),
                                  cudaMemcpyDeviceToHost, stream));
         SNN_CUDA(cudaStreamSynchronize(stream));

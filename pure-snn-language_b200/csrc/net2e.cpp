@@ -174,7 +174,7 @@ void build_layout(const HostNet& net, Layout& lay) {
     // groups: keys (d_eff, ff) per pre, ascending
     lay.gbeg.assign(N + 1, 0);
     std::vector<uint32_t> gid(S);
-    lay.gmeta.clear(); lay.gsize.clear(); lay.gu0.clear();
+    lay.gmeta.clear(); lay.gsize.clear(); lay.gu0.clear(); lay.gpre.clear();
     for (int pre = 0; pre < N; ++pre) {
         int slot[40];
         for (int q = 0; q < 40; ++q) slot[q] = -1;
@@ -192,6 +192,7 @@ void build_layout(const HostNet& net, Layout& lay) {
             lay.gsize.push_back(0);
             float u0 = (key & 1) ? 0.02f : (exc ? 0.2f : 0.05f);
             lay.gu0.push_back(u0);
+            lay.gpre.push_back(pre);
         }
         for (int64_t s = b; s < e; ++s) {
             int key = eff_delay(net.delay[s]) * 2 + ((net.flags[s] & RF_FF) ? 1 : 0);
@@ -201,6 +202,7 @@ void build_layout(const HostNet& net, Layout& lay) {
     }
     lay.gbeg[N] = (int32_t)lay.gmeta.size();
     lay.G = (int64_t)lay.gmeta.size();
+    SNN_REQUIRE(lay.G < (1ll << 30), SNN_ERR_ARG, "too many synapse groups for 30-bit ids");
     // post-major permutation, stable in synapse id
     lay.in_ptr.assign(N + 1, 0);
     for (int64_t s = 0; s < S; ++s) lay.in_ptr[net.post[s] + 1]++;
@@ -211,7 +213,8 @@ void build_layout(const HostNet& net, Layout& lay) {
     for (int64_t s = 0; s < S; ++s) {
         int32_t p = fill[net.post[s]]++;
         lay.perm[p] = (int32_t)s;
-        lay.gid_pm[p] = gid[s];
+        const uint32_t meta = lay.gmeta[gid[s]];
+        lay.gid_pm[p] = gid[s] | (((meta >> 5) & 1u) << 30) | (((meta >> 6) & 1u) << 31);
     }
 }
 

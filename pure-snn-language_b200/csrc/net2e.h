@@ -39,9 +39,10 @@ struct Layout {
     std::vector<uint32_t> gmeta;   // G: d_eff | ff<<5 | exc<<6
     std::vector<int32_t> gsize;    // G: synapses in the group
     std::vector<float> gu0;        // G: initial utilisation
+    std::vector<int32_t> gpre;     // G: pre-synaptic neuron of the group
     std::vector<int32_t> in_ptr;   // N+1
     std::vector<int32_t> perm;     // S: post-major position -> reference synapse id
-    std::vector<uint32_t> gid_pm;  // S: group of each post-major synapse
+    std::vector<uint32_t> gid_pm;  // S: group of each post-major synapse | FF << 30 | EXC << 31
 };
 void build_layout(const HostNet& net, Layout& lay);
 
