@@ -289,7 +289,7 @@ def main():
                        "l2": "inputs larger than L2 (synapse state ~0.73 GB per GPU)",
                        "events_per_step": arr / args.steps},
             "e2e": e2e,
-            "gpu_launches": int(sum(v["launches"] for v in prof["kernels"].values())),
+            "gpu_launches": int(sum(v["launches"] for n, v in prof["kernels"].items() if "@" not in n)),
             "kernels_ms_per_step": {k: v["ms"] / max(v["launches"], 1)
                                     for k, v in prof["kernels"].items()},
             "roofline": {"bound": "hbm", "kernel": "k_synapses", "achieved": achieved,

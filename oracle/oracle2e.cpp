@@ -31,10 +31,10 @@
 // CUDA path:
 //   (1) Float sums into a neuron (input current from arrivals, NMDA current)
 //       run over the neuron's incoming synapses in ascending reference
-//       synapse id (pre-major CSR index).  Terms of non-contributing synapses
-//       are +0.  Chunks of 32 consecutive incoming synapses are reduced by
-//       the xor butterfly (offsets 16,8,4,2,1); chunk results are added in
-//       order to an accumulator that starts at +0.
+//       synapse id (pre-major CSR index); non-contributing synapses give +0.
+//       Position k of that list goes to partial sum k mod 32; each partial
+//       adds its terms in ascending order from +0; the 32 partials are then
+//       reduced by the xor butterfly (offsets 16, 8, 4, 2, 1).
 //   (2) Every exponential is snn_expf (include/snn_pmath.h); constant decay
 //       factors are snn_expf of the same float argument the reference passes.
 //   (3) Contraction: an expression `a*b + c` (or `c + a*b`) that the
@@ -464,16 +464,18 @@ void setup(Oracle& o) {
     o.ht5_r = o.ne_r;
 }
 
-// canonical sum (1) over the incoming list of post j
+// canonical sum (1) over the incoming list of post j: 32 strided partial sums
+// (partial l adds incoming positions l, l+32, l+64, ... in ascending order,
+// starting from +0), then the xor butterfly over the 32 partials
 float canon_sum(const Oracle& o, int j, const std::vector<float>& term) {
     const int b = o.in_ptr[j], e = o.in_ptr[j + 1];
-    float acc = 0.0f;
-    for (int c = b; c < e; c += 32) {
-        float v[32];
-        for (int l = 0; l < 32; ++l) v[l] = (c + l < e) ? term[o.in_syn[c + l]] : 0.0f;
-        acc = pm_add(acc, tree32(v));
+    float v[32];
+    for (int l = 0; l < 32; ++l) {
+        float acc = 0.0f;
+        for (int p = b + l; p < e; p += 32) acc = pm_add(acc, term[o.in_syn[p]]);
+        v[l] = acc;
     }
-    return acc;
+    return tree32(v);
 }
 
 // M_ij = sigmoid(receptor . concentration), src/stage2e/synapse_kernels.cu:207-211

@@ -49,7 +49,8 @@ constexpr int TD_DIM = 200;
 
 // group view flag bits (view.w holds them as raw bits)
 constexpr uint32_t GV_D_MASK = 0x1f, GV_FF = 1u << 5, GV_EXC = 1u << 6, GV_ARR = 1u << 7,
-                   GV_NEXT = 1u << 8, GV_DISP = 1u << 9;
+                   GV_NEXT = 1u << 8, GV_DISP = 1u << 9,
+                   GV_EV = 1u << 10;  // arrival, dispatch or a ring read for the next step
 constexpr int NEU_BLOCK = 128;  // k_neurons CTA size; groups carry their pre's index in it
 // packed static group word: d_eff | ff << 5 | exc << 6 | size << 8 | (pre % NEU_BLOCK) << 24
 __host__ __device__ inline unsigned gw_size(unsigned m) { return (m >> 8) & 0xffffu; }
@@ -106,7 +107,8 @@ struct Dev {
     int* gsize;
     int* gpre;
     float4* gstate;  // R, u, nmda, xpre
-    float4* gview;   // nmda, xpre_ltp, R_dispatch, flags
+    float2* gview;   // hot view of step t: nmda, flags (as bits)
+    float2* gcold;   // cold view of step t: xpre before the arrival jump, R after STP
     // synapses (post-major)
     unsigned* gid;
     float* ca;
@@ -125,8 +127,8 @@ struct Dev {
     unsigned* raster;
     int raster_cap, words;
     int N, N_assoc, NPC, ncol, l4, per_sub;
-    const int* tile_post;  // n_tiles + 1 post boundaries of the synapse-pass tiles
-    int n_tiles, tile_cap;  // tiles; staged elements per stream per stage
+    int tile_cap;           // staged elements per stream per buffer (>= any aligned in-list)
+    int queue_cap;          // per-warp event queue entries (>= max in-degree)
 };
 
 __device__ __forceinline__ int phase_of(long long step) {
@@ -470,9 +472,12 @@ __global__ void __launch_bounds__(NEU_BLOCK) k_neurons(Dev d, Consts k) {
         }
         if (disp) disp_cnt += gw_size(meta);
         d.gstate[g] = st;
+        const bool ring = nxt && dd >= 2;
         const unsigned fl = (meta & (GV_D_MASK | GV_FF | GV_EXC)) | (arr ? GV_ARR : 0u) |
-                            (nxt ? GV_NEXT : 0u) | (disp ? GV_DISP : 0u);
-        d.gview[g] = make_float4(st.z, x_ltp, st.x, __uint_as_float(fl));
+                            (nxt ? GV_NEXT : 0u) | (disp ? GV_DISP : 0u) |
+                            ((arr || disp || ring) ? GV_EV : 0u);
+        d.gview[g] = make_float2(st.z, __uint_as_float(fl));
+        d.gcold[g] = make_float2(x_ltp, st.x);
     };
     // two groups per iteration keep independent loads in flight
     const int stride = 2 * blockDim.x;
@@ -512,96 +517,6 @@ __global__ void __launch_bounds__(NEU_BLOCK) k_neurons(Dev d, Consts k) {
 // reference synapse id, xor butterfly inside a chunk, chunks added in order.
 // Each lane carries two chunks at once (independent loads in flight).
 // ---------------------------------------------------------------------------
-struct PostCtx {
-    long long t;
-    float gain, prune, Mexc, Minh, Vj, mgj, xpost, one_m_V;
-    bool post_spk, e0, do10, do1000;
-    int slot_now;
-};
-
-__device__ __forceinline__ void synapse_one(const Dev& d, const Consts& k, const PostCtx& pc,
-                                            int p, unsigned gw, float4 v, float ca_in,
-                                            float& term_nmda, float& term_in) {
-    const unsigned fl = __float_as_uint(v.w);
-    const bool ff = gw & (1u << 30), exc = gw >> 31;
-    const int dd = fl & GV_D_MASK;
-    float ca = 0.0f;
-    if (exc) {
-        ca = pm_mul(ca_in, ff ? k.dec_ca_ff : k.dec_ca);
-        const float nm = pm_mul(v.x, pc.mgj);
-        ca = pm_fma(nm, k.ca_gain, ca);
-        const float cmax = ff ? k.ca_max_ff : k.ca_max;
-        if (ca > cmax) ca = cmax;
-        d.ca[p] = ca;
-        const float I = pm_mul(pm_mul(nm, pc.one_m_V), k.i_gain);
-        if (fabsf(I) > k.i_min) term_nmda = I;
-    }
-    const bool arr = fl & GV_ARR, disp = fl & GV_DISP, nxt = fl & GV_NEXT;
-    if (nxt && dd >= 2) {
-        const int sl = (int)(((pc.t + 1 - dd) / 3) & (VAL_SLOTS - 1));
-        term_in = d.val[(long long)p * VAL_SLOTS + sl];
-    }
-    if (pc.post_spk || arr || disp || pc.do10 || pc.do1000) {
-        float4 q = d.ev[p];  // alpha, beta, auto, elig
-        bool dirty = false;
-        const float eta = ff ? k.eta_ff : k.eta;
-        const float M = pc.e0 ? 1.0f : (exc ? pc.Mexc : pc.Minh);
-        const float pf = pc.e0 ? 1.0f : pm_sub(1.0f, pm_mul(0.5f, q.z));
-        if (pc.post_spk) {  // LTP from the pre trace (post spiked)
-            const float dw = pm_fma(v.y, k.a_plus, 0.0f);
-            if (dw > 0.0f) q.x = pm_fma(pm_mul(pm_mul(pm_mul(eta, dw), pc.gain), M), pf, q.x);
-            if (ca > k.reb_thr) {
-                const float ex = pm_sub(ca, k.reb_thr);
-                q.y = pm_fma(pm_mul(pm_mul(pm_mul(eta, ex), k.reb_gain), pc.gain), M, q.y);
-            }
-            q.w = pm_add(q.w, dw);
-            dirty = true;
-        }
-        if (arr) {  // LTD at arrival from the post trace
-            const float dw = pm_mul(-pc.xpost, k.a_minus);
-            if (dw < 0.0f) q.y = pm_fma(pm_mul(pm_mul(pm_mul(eta, -dw), pc.gain), M), pf, q.y);
-            q.w = pm_add(q.w, dw);
-            dirty = true;
-        }
-        if (disp) {  // value this dispatch delivers d steps later
-            const float wm = pm_div(pm_mul(k.w_max, q.x), pm_add(q.x, q.y));
-            const float val = pm_mul(exc ? wm : -wm, v.z);
-            if (dd == 1) term_in = val;
-            else d.val[(long long)p * VAL_SLOTS + pc.slot_now] = val;
-        }
-        if (pc.do10) {
-            if (exc) {
-                float act = d.act[p], au = q.z;
-                const float ca4 = pm_mul(pm_mul(pm_mul(ca, ca), ca), ca);
-                const float da = pm_fma(pm_mul(k.ck_k1, ca4), pm_sub(1.0f, act),
-                                        -pm_mul(pm_mul(k.ck_k2, act), k.ck_pp1));
-                const float du = pm_fma(pm_mul(pm_mul(k.ck_k3, act), act), pm_sub(1.0f, au),
-                                        -pm_mul(pm_mul(k.ck_k4, au), k.ck_pp1));
-                act = clampf(pm_fma(da, k.ck_dt, act), 0.0f, 1.0f);
-                au = clampf(pm_fma(du, k.ck_dt, au), 0.0f, 1.0f);
-                d.act[p] = act;
-                q.z = au;
-            }
-            const float a1 = pm_fma(d.e1[p], k.e1_dec, q.w);
-            const float a2 = pm_fma(d.e2[p], k.e2_dec, a1);
-            d.e1[p] = a1;
-            d.e2[p] = a2;
-            q.w = 0.0f;
-            dirty = true;
-        }
-        if (pc.do1000) {
-            float a = pm_mul(q.x, k.psw_decay), bb = pm_mul(q.y, k.psw_decay);
-            if (a < k.ab_min) a = k.ab_min;
-            if (bb < k.ab_min) bb = k.ab_min;
-            if (pm_add(a, bb) < pc.prune) { a = k.ab_reset; bb = k.ab_reset; }
-            q.x = a;
-            q.y = bb;
-            dirty = true;
-        }
-        if (dirty) d.ev[p] = q;
-    }
-}
-
 // --- bulk async copy (1D TMA) helpers -------------------------------------
 __device__ __forceinline__ unsigned smem_u32(const void* p) {
     return static_cast<unsigned>(__cvta_generic_to_shared(p));
@@ -634,32 +549,169 @@ __device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, unsigned 
     return ok != 0;
 }
 
-constexpr int SYN_THREADS = 512;       // 16 warps per CTA
+#ifndef SYN_UNROLL
+#define SYN_UNROLL 4   // 32-synapse chunks whose loads a warp issues together
+#endif
+#ifndef SYN_MIN_BLOCKS
+#define SYN_MIN_BLOCKS 3
+#endif
+constexpr int SYN_THREADS = 256;       // 8 warps per CTA, each an independent pipeline
 constexpr int SYN_WARPS = SYN_THREADS / 32;
 constexpr unsigned WAIT_LIMIT = 1u << 24;  // bounded spin (~seconds) before flagging an error
 
-// one tile = consecutive post-synaptic neurons [tile_post[k], tile_post[k+1])
-// whose incoming synapses [in_ptr[j0], in_ptr[j1]) fit the staging buffers
-__device__ __forceinline__ void tile_range(const Dev& d, int tile, int& j0, int& j1, int& a0,
-                                           int& a1) {
-    j0 = d.tile_post[tile];
-    j1 = d.tile_post[tile + 1];
-    a0 = d.in_ptr[j0] & ~3;
-    a1 = (d.in_ptr[j1] + 3) & ~3;
+struct PostCtx {
+    long long t;
+    float gain, prune, Mexc, Minh, mgj, xpost, one_m_V;
+    bool post_spk, e0, do10, do1000;
+    int slot_now;
+};
+
+// Plasticity / dispatch / periodic work of one queued synapse p (every
+// synapse of a spiking post, arrivals, dispatches, ring reads, and all
+// synapses on the 10- / 1000-step schedule).  Returns the synapse's term of
+// the next step's input current (0 if none).
+// Plasticity / dispatch / periodic work of one queued synapse, split into a
+// load stage (all independent loads issued) and a compute stage, so that a
+// warp can keep two batches of 32 queued synapses in flight.
+struct EvIn {
+    unsigned gw, fl;
+    int p;
+    float ca, ring, act, e1, e2;
+    float2 cold;
+    float4 q;
+};
+
+__device__ __forceinline__ void ev_load(const Dev& d, const PostCtx& pc, int p, unsigned gw,
+                                        unsigned fl, float ca, EvIn& x) {
+    x.gw = gw; x.fl = fl; x.p = p; x.ca = ca;
+    const int dd = fl & GV_D_MASK;
+    const bool plast = pc.post_spk || (fl & (GV_ARR | GV_DISP)) || pc.do10 || pc.do1000;
+    x.ring = 0.0f;
+    if ((fl & GV_NEXT) && dd >= 2)
+        x.ring = d.val[(long long)p * VAL_SLOTS + (int)(((pc.t + 1 - dd) / 3) & (VAL_SLOTS - 1))];
+    x.cold = make_float2(0.0f, 0.0f);
+    x.q = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    x.act = x.e1 = x.e2 = 0.0f;
+    if (plast) {
+        x.cold = d.gcold[gw & 0x3fffffffu];  // x_pre before the arrival jump, R after STP
+        x.q = d.ev[p];                       // alpha, beta, auto, elig
+        if (pc.do10) {
+            if (gw >> 31) x.act = d.act[p];
+            x.e1 = d.e1[p];
+            x.e2 = d.e2[p];
+        }
+    }
 }
 
-__global__ void __launch_bounds__(SYN_THREADS) k_synapses(Dev d, Consts k) {
+// returns the synapse's term of the next step's input current (0 if none)
+__device__ __forceinline__ float ev_compute(const Dev& d, const Consts& k, const PostCtx& pc,
+                                            EvIn& x) {
+    const unsigned fl = x.fl;
+    const bool ff = x.gw & (1u << 30), exc = x.gw >> 31;
+    const int dd = fl & GV_D_MASK;
+    const bool arr = fl & GV_ARR, disp = fl & GV_DISP;
+    const bool plast = pc.post_spk || arr || disp || pc.do10 || pc.do1000;
+    float term_in = x.ring;
+    if (!plast) return term_in;
+    float4 q = x.q;
+    const float ca = x.ca;
+    const int p = x.p;
+    const float eta = ff ? k.eta_ff : k.eta;
+    const float M = pc.e0 ? 1.0f : (exc ? pc.Mexc : pc.Minh);
+    const float pf = pc.e0 ? 1.0f : pm_sub(1.0f, pm_mul(0.5f, q.z));
+    if (pc.post_spk) {  // LTP from the pre trace (post spiked)
+        const float dw = pm_fma(x.cold.x, k.a_plus, 0.0f);
+        if (dw > 0.0f) q.x = pm_fma(pm_mul(pm_mul(pm_mul(eta, dw), pc.gain), M), pf, q.x);
+        if (ca > k.reb_thr) {
+            const float ex = pm_sub(ca, k.reb_thr);
+            q.y = pm_fma(pm_mul(pm_mul(pm_mul(eta, ex), k.reb_gain), pc.gain), M, q.y);
+        }
+        q.w = pm_add(q.w, dw);
+    }
+    if (arr) {  // LTD at arrival from the post trace
+        const float dw = pm_mul(-pc.xpost, k.a_minus);
+        if (dw < 0.0f) q.y = pm_fma(pm_mul(pm_mul(pm_mul(eta, -dw), pc.gain), M), pf, q.y);
+        q.w = pm_add(q.w, dw);
+    }
+    if (disp) {  // value this dispatch delivers d steps later
+        const float wm = pm_div(pm_mul(k.w_max, q.x), pm_add(q.x, q.y));
+        const float val = pm_mul(exc ? wm : -wm, x.cold.y);
+        if (dd == 1) term_in = val;
+        else d.val[(long long)p * VAL_SLOTS + pc.slot_now] = val;
+    }
+    if (pc.do10) {
+        if (exc) {
+            float act = x.act, au = q.z;
+            const float ca4 = pm_mul(pm_mul(pm_mul(ca, ca), ca), ca);
+            const float da = pm_fma(pm_mul(k.ck_k1, ca4), pm_sub(1.0f, act),
+                                    -pm_mul(pm_mul(k.ck_k2, act), k.ck_pp1));
+            const float du = pm_fma(pm_mul(pm_mul(k.ck_k3, act), act), pm_sub(1.0f, au),
+                                    -pm_mul(pm_mul(k.ck_k4, au), k.ck_pp1));
+            act = clampf(pm_fma(da, k.ck_dt, act), 0.0f, 1.0f);
+            au = clampf(pm_fma(du, k.ck_dt, au), 0.0f, 1.0f);
+            d.act[p] = act;
+            q.z = au;
+        }
+        const float a1 = pm_fma(x.e1, k.e1_dec, q.w);
+        const float a2 = pm_fma(x.e2, k.e2_dec, a1);
+        d.e1[p] = a1;
+        d.e2[p] = a2;
+        q.w = 0.0f;
+    }
+    if (pc.do1000) {
+        float a = pm_mul(q.x, k.psw_decay), bb = pm_mul(q.y, k.psw_decay);
+        if (a < k.ab_min) a = k.ab_min;
+        if (bb < k.ab_min) bb = k.ab_min;
+        if (pm_add(a, bb) < pc.prune) { a = k.ab_reset; bb = k.ab_reset; }
+        q.x = a;
+        q.y = bb;
+    }
+    if (pc.post_spk || arr || pc.do10 || pc.do1000) d.ev[p] = q;
+    return term_in;
+}
+
+__device__ __forceinline__ void prefetch_l2(const void* ptr) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
+}
+
+// ---------------------------------------------------------------------------
+// k_synapses: persistent; every warp is an independent pipeline over the
+// post-synaptic neurons j = w, w + W, w + 2W, ... (w its global warp index, W
+// the number of warps).  Lane 0 stages the group ids and Ca values of the
+// warp's next neuron into the warp's own shared-memory buffer with
+// cp.async.bulk (mbarrier per buffer, two buffers) while the warp works on
+// the current one.  Per neuron:
+//   dense phase ..... Ca / NMDA (synapse_kernels.cu:45-121) for every incoming
+//                     synapse (four 32-synapse chunks per iteration); synapses
+//                     that also need plasticity, dispatch or ring work go to a
+//                     per-warp queue
+//   event phase ..... the queue, 32 synapses at a time: LTP (post spike,
+//                     synapse_kernels.cu:153-255), LTD (arrival, :257-329),
+//                     dispatch capture (neuron_kernels.cu:204-206), ring read
+//                     (delivery at t+1, neuron_kernels.cu:37-56), CaMKII /
+//                     eligibility (t % 10, synapse_kernels.cu:469-543), PSW
+//                     decay (t % 1000, scheduler.cu:55-86)
+// Sums (NMDA current, next-step input) follow the canonical order: lane l
+// keeps the partial of positions l, l+32, ... in ascending order (zero terms
+// skipped, which is exact), then one xor butterfly.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d, Consts k) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    __shared__ __align__(8) unsigned long long bars[2];
-    unsigned* const sbase = reinterpret_cast<unsigned*>(smem_raw);
-    const int cap = d.tile_cap;  // stage s: gid at sbase + 2*cap*s, ca right after it
+    __shared__ __align__(8) unsigned long long bars[SYN_WARPS][2];
     if (blockIdx.x == 0 && threadIdx.x == 0) step_epilogue(d, k);
-    if (threadIdx.x == 0) {
-        mbar_init(&bars[0], 1);
-        mbar_init(&bars[1], 1);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const unsigned lt_mask = (1u << lane) - 1u;
+    const int cap = d.tile_cap;  // staged elements per stream per buffer
+    // per-warp shared memory: [buf0 gid | buf0 ca | buf1 gid | buf1 ca | queue]
+    unsigned* const wbase = reinterpret_cast<unsigned*>(smem_raw) + (size_t)warp * (4 * cap + d.queue_cap);
+    unsigned* const queue = wbase + 4 * cap;  // position | flags << 16
+    unsigned long long* const bar = bars[warp];
+    if (lane == 0) {
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    __syncthreads();
+    __syncwarp();
     const Ctrl* c = d.ctrl;
     PostCtx pc;
     pc.t = c->t;
@@ -671,88 +723,136 @@ __global__ void __launch_bounds__(SYN_THREADS) k_synapses(Dev d, Consts k) {
     pc.do10 = (pc.t % 10 == 0) && !pc.e0;
     pc.do1000 = (pc.t % 1000 == 0);
     pc.slot_now = (int)((pc.t / 3) & (VAL_SLOTS - 1));
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    // thread 0 only: stage the gid / ca streams of `tile` into buffer `stage`
-    auto issue = [&](int tile, int stage) {
-        int j0, j1, a0, a1;
-        tile_range(d, tile, j0, j1, a0, a1);
+    const bool all_events = pc.do10 || pc.do1000;
+    const int W = gridDim.x * SYN_WARPS;
+    const int w = blockIdx.x * SYN_WARPS + warp;
+    auto issue = [&](int j, int buf) {  // lane 0 only
+        const int a0 = d.in_ptr[j] & ~3, a1 = (d.in_ptr[j + 1] + 3) & ~3;
         const unsigned bytes = (unsigned)(a1 - a0) * 4u;
-        unsigned* dst = sbase + 2 * cap * stage;
+        unsigned* dst = wbase + 2 * cap * buf;
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        mbar_expect_tx(&bars[stage], 2u * bytes);
+        mbar_expect_tx(&bar[buf], 2u * bytes);
         if (bytes > 0) {
-            bulk_g2s(dst, d.gid + a0, bytes, &bars[stage]);
-            bulk_g2s(dst + cap, d.ca + a0, bytes, &bars[stage]);
+            bulk_g2s(dst, d.gid + a0, bytes, &bar[buf]);
+            bulk_g2s(dst + cap, d.ca + a0, bytes, &bar[buf]);
         }
     };
-    unsigned phases = 0u;  // bit s = parity of the next wait on stage s
+    unsigned phases = 0u;  // bit s = parity of the next wait on buffer s
     int it = 0;
-    if (threadIdx.x == 0 && (int)blockIdx.x < d.n_tiles) issue(blockIdx.x, 0);
-    for (int tile = blockIdx.x; tile < d.n_tiles; tile += gridDim.x, ++it) {
-        const int stage = it & 1;
-        const int next = tile + gridDim.x;
-        if (threadIdx.x == 0 && next < d.n_tiles) issue(next, stage ^ 1);
-        // wait for this tile's streams (bounded)
+    if (lane == 0 && w < d.N) issue(w, 0);
+    for (int j = w; j < d.N; j += W, ++it) {
+        const int buf = it & 1;
+        const int next = j + W;
+        if (lane == 0 && next < d.N) issue(next, buf ^ 1);
         bool ok = false;
         for (unsigned spin = 0; spin < WAIT_LIMIT; ++spin) {
-            if (mbar_try_wait(&bars[stage], (phases >> stage) & 1u)) { ok = true; break; }
+            if (mbar_try_wait(&bar[buf], (phases >> buf) & 1u)) { ok = true; break; }
         }
-        phases ^= 1u << stage;
-        if (__syncthreads_or(!ok)) {
-            if (threadIdx.x == 0) {
+        phases ^= 1u << buf;
+        if (__any_sync(0xffffffffu, !ok)) {
+            if (lane == 0) {
                 atomicOr(&d.ctrl->error, 1);
-                // drain the copy already issued for the next tile (bounded) before exiting
-                if (next < d.n_tiles)
+                if (next < d.N)  // drain the copy already issued (bounded) before exiting
                     for (unsigned spin = 0; spin < WAIT_LIMIT; ++spin)
-                        if (mbar_try_wait(&bars[stage ^ 1], (phases >> (stage ^ 1)) & 1u)) break;
+                        if (mbar_try_wait(&bar[buf ^ 1], (phases >> (buf ^ 1)) & 1u)) break;
             }
             return;
         }
-        int j0, j1, a0, a1;
-        tile_range(d, tile, j0, j1, a0, a1);
-        const unsigned* sg = sbase + 2 * cap * stage;
-        const float* sc = reinterpret_cast<const float*>(sg + cap);
-        for (int j = j0 + warp; j < j1; j += SYN_WARPS) {
-            pc.Vj = d.V[j];
-            pc.mgj = d.mg[j];
-            pc.post_spk = d.hist[j] & 1u;
-            pc.xpost = d.xpost[j];
-            pc.one_m_V = pm_sub(k.e_rev, pc.Vj);
-            const int b = d.in_ptr[j], e = d.in_ptr[j + 1];
-            float acc_nmda = 0.0f, acc_in = 0.0f;
-            for (int base = b; base < e; base += 64) {
-                const int p0 = base + lane, p1 = base + 32 + lane;
-                const bool v0 = p0 < e, v1 = p1 < e;
-                const unsigned gw0 = v0 ? sg[p0 - a0] : 0u;
-                const unsigned gw1 = v1 ? sg[p1 - a0] : 0u;
-                const float ca0 = v0 ? sc[p0 - a0] : 0.0f;
-                const float ca1 = v1 ? sc[p1 - a0] : 0.0f;
-                const float4 w0 = v0 ? d.gview[gw0 & 0x3fffffffu] : make_float4(0, 0, 0, 0);
-                const float4 w1 = v1 ? d.gview[gw1 & 0x3fffffffu] : make_float4(0, 0, 0, 0);
-                float n0 = 0.0f, i0 = 0.0f, n1 = 0.0f, i1 = 0.0f;
-                if (v0) synapse_one(d, k, pc, p0, gw0, w0, ca0, n0, i0);
-                if (v1) synapse_one(d, k, pc, p1, gw1, w1, ca1, n1, i1);
+        const int b = d.in_ptr[j], e = d.in_ptr[j + 1];
+        const int a0 = b & ~3;
+        const unsigned* sg = wbase + 2 * cap * buf;
+        float* sc = reinterpret_cast<float*>(wbase + 2 * cap * buf + cap);
+        pc.mgj = d.mg[j];
+        pc.post_spk = d.hist[j] & 1u;
+        pc.xpost = d.xpost[j];
+        pc.one_m_V = pm_sub(k.e_rev, d.V[j]);
+        const bool all = all_events || pc.post_spk;
+        float part_nmda = 0.0f, part_in = 0.0f;
+        int qn = 0;
+        // dense phase: four chunks per iteration, all loads issued first
+        constexpr int U = SYN_UNROLL;
+        for (int base = b; base < e; base += 32 * U) {
+            unsigned gw[U];
+            float2 hv[U];
+            float cav[U];
 #pragma unroll
-                for (int o = 16; o >= 1; o >>= 1) {
-                    n0 = pm_add(n0, __shfl_xor_sync(0xffffffffu, n0, o));
-                    i0 = pm_add(i0, __shfl_xor_sync(0xffffffffu, i0, o));
-                    n1 = pm_add(n1, __shfl_xor_sync(0xffffffffu, n1, o));
-                    i1 = pm_add(i1, __shfl_xor_sync(0xffffffffu, i1, o));
-                }
-                acc_nmda = pm_add(acc_nmda, n0);
-                acc_in = pm_add(acc_in, i0);
-                if (base + 32 < e) {
-                    acc_nmda = pm_add(acc_nmda, n1);
-                    acc_in = pm_add(acc_in, i1);
-                }
+            for (int h = 0; h < U; ++h) {
+                const int p = base + 32 * h + lane;
+                gw[h] = p < e ? sg[p - a0] : 0u;
+                cav[h] = p < e ? sc[p - a0] : 0.0f;
             }
-            if (lane == 0) {
-                d.nmda_cur[j] = acc_nmda;
-                d.input[j] = acc_in;
+#pragma unroll
+            for (int h = 0; h < U; ++h) {
+                const int p = base + 32 * h + lane;
+                hv[h] = p < e ? d.gview[gw[h] & 0x3fffffffu] : make_float2(0.0f, 0.0f);
+            }
+#pragma unroll
+            for (int h = 0; h < U; ++h) {
+                const int p = base + 32 * h + lane;
+                const bool v = p < e;
+                const unsigned fl = __float_as_uint(hv[h].y);
+                const bool need = v && (all || (fl & GV_EV));
+                if (v && (gw[h] >> 31)) {  // excitatory: Ca and NMDA current
+                    const bool ff = gw[h] & (1u << 30);
+                    float ca = pm_mul(cav[h], ff ? k.dec_ca_ff : k.dec_ca);
+                    const float nm = pm_mul(hv[h].x, pc.mgj);
+                    ca = pm_fma(nm, k.ca_gain, ca);
+                    const float cmax = ff ? k.ca_max_ff : k.ca_max;
+                    if (ca > cmax) ca = cmax;
+                    if (need) sc[p - a0] = ca;  // read back by the event phase
+                    d.ca[p] = ca;
+                    const float I = pm_mul(pm_mul(nm, pc.one_m_V), k.i_gain);
+                    if (fabsf(I) > k.i_min) part_nmda = pm_add(part_nmda, I);
+                }
+                const unsigned m = __ballot_sync(0xffffffffu, need);
+                if (need) queue[qn + __popc(m & lt_mask)] = (unsigned)(p - b) | (fl << 16);
+                qn += __popc(m);
             }
         }
-        // every thread is done with this stage before it is refilled
-        __syncthreads();
+        __syncwarp();
+        // event phase: two batches of 32 queued synapses in flight, ascending
+        auto accumulate = [&](float term, int off) {
+            unsigned m = __ballot_sync(0xffffffffu, term != 0.0f);
+            while (m) {
+                const int src = __ffs(m) - 1;
+                m &= m - 1;
+                const int o = __shfl_sync(0xffffffffu, off, src);
+                const float tv = __shfl_sync(0xffffffffu, term, src);
+                if ((o & 31) == lane) part_in = pm_add(part_in, tv);
+            }
+        };
+        for (int q0 = 0; q0 < qn; q0 += 64) {
+            const int qa = q0 + lane, qb = q0 + 32 + lane;
+            EvIn xa, xb;
+            int offa = 0, offb = 0;
+            if (qa < qn) {
+                const unsigned ent = queue[qa];
+                offa = (int)(ent & 0xffffu);
+                const int p = b + offa;
+                ev_load(d, pc, p, sg[p - a0], ent >> 16, sc[p - a0], xa);
+            }
+            if (qb < qn) {
+                const unsigned ent = queue[qb];
+                offb = (int)(ent & 0xffffu);
+                const int p = b + offb;
+                ev_load(d, pc, p, sg[p - a0], ent >> 16, sc[p - a0], xb);
+            }
+            const float ta = qa < qn ? ev_compute(d, k, pc, xa) : 0.0f;
+            const float tb = qb < qn ? ev_compute(d, k, pc, xb) : 0.0f;
+            accumulate(ta, offa);
+            if (q0 + 32 < qn) accumulate(tb, offb);
+        }
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) {
+            part_nmda = pm_add(part_nmda, __shfl_xor_sync(0xffffffffu, part_nmda, o));
+            part_in = pm_add(part_in, __shfl_xor_sync(0xffffffffu, part_in, o));
+        }
+        if (lane == 0) {
+            d.nmda_cur[j] = part_nmda;
+            d.input[j] = part_in;
+        }
+        // the whole warp is done with this buffer before lane 0 refills it
+        __syncwarp();
     }
 }
 
@@ -783,15 +883,14 @@ struct Engine2e : snnb::Engine {
         neuron_byte_counts;
     snnb::DevBuf<unsigned short> off;
     snnb::DevBuf<unsigned> info, hist, gmeta, gid, byte_hist_nov, raster;
-    snnb::DevBuf<float4> gstate, gview, ev, gates;
+    snnb::DevBuf<float4> gstate, ev, gates;
+    snnb::DevBuf<float2> gview, gcold;
     snnb::DevBuf<float> w_value, w_pred, baseline;
     snnb::DevBuf<Ctrl> ctrl;
     snnb::DevBuf<unsigned char> corpus;
     snnb::DevBuf<int> counts_tmp;
-    snnb::DevBuf<int> tile_post;
-    int n_tiles = 0, tile_cap = 0, syn_grid = 1;
+    int tile_cap = 0, syn_grid = 1, queue_cap = 0;
     size_t syn_smem = 0;
-    static constexpr int TILE_POSTS = 16;
 
     explicit Engine2e(const snn_config& c) : cfg(c) {
         if (cfg.raster_steps > 0) raster_cap = cfg.raster_steps;
@@ -882,7 +981,7 @@ struct Engine2e : snnb::Engine {
         gbeg.upload(lay.gbeg.data(), N + 1, stream);
         in_ptr.upload(lay.in_ptr.data(), N + 1, stream);
         // groups
-        gmeta.alloc(G); gsize.alloc(G); gstate.alloc(G); gview.alloc(G);
+        gmeta.alloc(G); gsize.alloc(G); gstate.alloc(G); gview.alloc(G); gcold.alloc(G);
         {
             std::vector<unsigned> packed(G);
             for (int64_t g = 0; g < G; ++g) {
@@ -899,44 +998,39 @@ struct Engine2e : snnb::Engine {
         for (int64_t g = 0; g < G; ++g) h_gs[g] = make_float4(1.0f, lay.gu0[g], 0.0f, 0.0f);
         gstate.upload(h_gs.data(), G, stream);
         gview.zero(stream);
+        gcold.zero(stream);
         // synapses, post-major
         // gid / ca are streamed in 16-byte aligned tiles: pad by 4 elements
         gid.alloc(S + 4); ca.alloc(S + 4); ev.alloc(S); act.alloc(S); e1.alloc(S); e2.alloc(S);
         val.alloc((size_t)S * VAL_SLOTS);
         gid.zero(stream);
         gid.upload(lay.gid_pm.data(), S, stream);
-        // synapse-pass tiles: TILE_POSTS consecutive post neurons each
-        {
-            std::vector<int> tp;
-            int cap = 4;
-            for (int j0 = 0; j0 < N; j0 += TILE_POSTS) {
-                const int j1 = std::min(N, j0 + TILE_POSTS);
-                tp.push_back(j0);
-                const int a0 = lay.in_ptr[j0] & ~3, a1 = (lay.in_ptr[j1] + 3) & ~3;
-                cap = std::max(cap, a1 - a0);
-            }
-            tp.push_back(N);
-            n_tiles = (int)tp.size() - 1;
-            tile_cap = (cap + 3) & ~3;
-            tile_post.alloc(tp.size());
-            tile_post.upload(tp.data(), tp.size(), stream);
-            const size_t smem = (size_t)4 * tile_cap * sizeof(unsigned);
-            SNN_REQUIRE(smem <= 200 * 1024, SNN_ERR_ARG, "synapse tile exceeds shared memory");
-            SNN_CUDA(cudaFuncSetAttribute(k_synapses, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)smem));
-            int sms = 0;
-            SNN_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, cfg.device));
-            syn_grid = std::min(n_tiles, 2 * sms);
-            syn_smem = smem;
-        }
-        {
+        {   // plasticity records {alpha, beta, auto, elig}, post-major
             std::vector<float4> h_ev(S);
             for (int64_t p = 0; p < S; ++p) {
-                int32_t sid = lay.perm[p];
+                const int32_t sid = lay.perm[p];
                 h_ev[p] = make_float4(net.alpha[sid], net.beta[sid], 0.0f, 0.0f);
             }
             ev.upload(h_ev.data(), S, stream);
             SNN_CUDA(cudaStreamSynchronize(stream));
+        }
+        // synapse pass: per-warp staging buffers sized by the largest in-degree
+        {
+            int max_in = 0;
+            for (int j = 0; j < N; ++j) max_in = std::max(max_in, lay.in_ptr[j + 1] - lay.in_ptr[j]);
+            SNN_REQUIRE(max_in < 65536, SNN_ERR_ARG, "in-degree above 65535");
+            tile_cap = ((max_in + 6) + 3) & ~3;   // aligned range of any neuron's list
+            queue_cap = (max_in + 31) & ~31;
+            const size_t smem = (size_t)SYN_WARPS * (4 * (size_t)tile_cap + queue_cap) * sizeof(unsigned);
+            SNN_REQUIRE(smem <= 200 * 1024, SNN_ERR_ARG, "in-degree too large for the staging buffers");
+            SNN_CUDA(cudaFuncSetAttribute(k_synapses, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)smem));
+            int sms = 0, per_sm = 0;
+            SNN_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, cfg.device));
+            SNN_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_synapses, SYN_THREADS, smem));
+            per_sm = std::max(per_sm, 1);
+            syn_grid = std::max(1, std::min((N + SYN_WARPS - 1) / SYN_WARPS, per_sm * sms));
+            syn_smem = smem;
         }
         ca.zero(stream); act.zero(stream); e1.zero(stream); e2.zero(stream); val.zero(stream);
         // control
@@ -969,8 +1063,8 @@ struct Engine2e : snnb::Engine {
         D.V = V.p; D.wad = wad.p; D.s = s.p; D.fr = fr.p; D.can = can.p; D.xpost = xpost.p; D.mg = mg.p;
         D.input = input.p; D.nmda_cur = nmda_cur.p; D.last = last.p; D.ref = ref.p; D.off = off.p;
         D.info = info.p; D.hist = hist.p; D.gbeg = gbeg.p; D.in_ptr = in_ptr.p;
-        D.gmeta = gmeta.p; D.gsize = gsize.p; D.gpre = gpre.p; D.gstate = gstate.p; D.gview = gview.p;
-        D.tile_post = tile_post.p; D.n_tiles = n_tiles; D.tile_cap = tile_cap;
+        D.gmeta = gmeta.p; D.gsize = gsize.p; D.gpre = gpre.p; D.gstate = gstate.p; D.gview = gview.p; D.gcold = gcold.p;
+        D.tile_cap = tile_cap; D.queue_cap = queue_cap;
         D.gid = gid.p; D.ca = ca.p; D.ev = ev.p; D.act = act.p; D.e1 = e1.p; D.e2 = e2.p; D.val = val.p;
         D.ctrl = ctrl.p; D.gates = gates.p; D.col_sp = col_sp.p; D.l6_sp = l6_sp.p; D.sub_sp = sub_sp.p;
         D.byte_hist_nov = byte_hist_nov.p; D.byte_histogram = byte_histogram.p;
@@ -1031,7 +1125,10 @@ struct Engine2e : snnb::Engine {
     }
 
     // accumulate the profile of n steps whose events are pev[0 .. 3n]
-    void harvest(int n) {
+    // accumulate the profile of n steps starting at step t0; slot 3 also
+    // collects the synapse pass of steps with t % 10 == 0 (CaMKII /
+    // eligibility schedule), which move most bytes
+    void harvest(int n, long long t0) {
         SNN_CUDA(cudaStreamSynchronize(stream));
         for (int q = 0; q < n; ++q) {
             for (int kk = 0; kk < 3; ++kk) {
@@ -1040,6 +1137,10 @@ struct Engine2e : snnb::Engine {
                 prof.kernel_ms[kk] += ms;
                 prof.launches[kk] += 1;
                 prof.step_ms += ms;
+                if (kk == 2 && (t0 + q) % 10 == 0) {
+                    prof.kernel_ms[3] += ms;
+                    prof.launches[3] += 1;
+                }
             }
         }
         prof.steps += n;
@@ -1063,10 +1164,11 @@ struct Engine2e : snnb::Engine {
         profiling = en != 0;
         drop_graph();
         memset(&prof, 0, sizeof(prof));
-        prof.n_kernels = 3;
+        prof.n_kernels = 4;
         strcpy(prof.names[0], "k_control");
         strcpy(prof.names[1], "k_neurons");
         strcpy(prof.names[2], "k_synapses");
+        strcpy(prof.names[3], "k_synapses@t%10==0");
     }
 
     void get_profile(snn_profile* o) override { *o = prof; }
@@ -1100,13 +1202,13 @@ struct Engine2e : snnb::Engine {
                 if (span - q >= chunk) {
                     ensure_graph(chunk);
                     SNN_CUDA(cudaGraphLaunch(graph_exec, stream));
-                    if (profiling) harvest(chunk);
+                    if (profiling) harvest(chunk, steps + done + q);
                     q += chunk;
                 } else {
                     if (profiling) ensure_events(1);
                     launch_step(stream, profiling ? &pev[0] : nullptr);
                     SNN_CUDA(cudaGetLastError());
-                    if (profiling) harvest(1);
+                    if (profiling) harvest(1, steps + done + q);
                     q += 1;
                 }
             }
