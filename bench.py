@@ -150,6 +150,112 @@ def cpu_baseline(warmup, budget_s=12.0, threads=0):
                       f"CPU oracle, {cores} OpenMP threads"}
 
 
+PROP_RATES = (0.001, 0.01, 0.03, 0.1)
+PROP_MODES = ((0, "STDP off"), (1, "STDP on"), (2, "STP on"))
+
+
+def prop_push_bytes(events, pre_spikes, mode):
+    """Algorithmic HBM bytes of the push kernel: post + weight streams (8 B
+    per event), the spike list (4 B per spiker, +4 release with STP), the
+    LTD weight write-back (4 B per event of the 80 % excitatory pres)."""
+    b = 8.0 * events + 4.0 * pre_spikes
+    if mode & 2:
+        b += 4.0 * pre_spikes
+    if mode & 1:
+        b += 4.0 * 0.8 * events
+    return b
+
+
+def prop_cpu_baseline(rate, budget_s=10.0):
+    """CPU oracle of the microbench (plain propagation, 1 M x 1,000) timed on
+    all host cores for a bounded number of steps."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import pyoracle as po
+    cores = os.cpu_count()
+    o = po.Oracle4(po.prop_params(n=1_000_000, fanout=1000, rate=rate, mode=0, n_threads=cores))
+    o.run(3)
+    c0 = o.counters()
+    t0 = time.perf_counter()
+    n = 0
+    while n < 5 or time.perf_counter() - t0 < budget_s:
+        o.run(1)
+        n += 1
+    dt = time.perf_counter() - t0
+    ev = o.counters()["events"] - c0["events"]
+    o.close()
+    return {"value": ev / dt, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"{n} steps of the 1M x 1,000 microbench at rate {rate} (STDP off), "
+                      f"CPU oracle, {cores} OpenMP threads"}
+
+
+def prop_main(args):
+    """Propagation microbench: one JSON line per (mode, rate)."""
+    import snn_b200 as snn
+    import torch
+    warm = max(args.warmup, 3)
+    peak, peak_kind = measured_peaks()
+    cb = None if args.no_cpu_baseline else prop_cpu_baseline(0.01)
+    for mode, mname in PROP_MODES:
+        for rate in PROP_RATES:
+            net = snn.Network(model=snn.MODEL_PROP, prop_mode=mode, prop_rate=rate)
+            net.build_columns(snn.topology(snn.MODEL_PROP))
+            net.run(warm)
+            net.synchronize()
+            c0 = net.counters()
+            torch.cuda.synchronize()
+            net.set_profiling(True)
+            with ClockSampler(0) as clk:
+                net.run(args.steps)
+                net.synchronize()
+            prof = net.profile()
+            net.set_profiling(False)
+            c1 = net.counters()
+            ev = c1["arrivals"] - c0["arrivals"]
+            pre = c1["dispatched"] - c0["dispatched"]
+            dev_s = prof["step_ms"] / 1000.0
+            push = prof["kernels"]["k4_push"]
+            push_s = push["ms"] / push["launches"] / 1000.0
+            pb = prop_push_bytes(ev, pre, mode) / args.steps
+            achieved = pb / push_s / 1e9
+            # end to end: snn_run with the spike raster copied to pinned host memory
+            raster = torch.empty((args.steps, net.words), dtype=torch.int32, pin_memory=True)
+            ce0 = net.counters()
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            net._check(net.L.snn_run(net.h, args.steps, None, 0, 1, raster.data_ptr(), None))
+            net.synchronize()
+            wall = time.perf_counter() - t0
+            e2e_ev = net.counters()["arrivals"] - ce0["arrivals"]
+            line = {
+                "metric": "synaptic events/sec (SOPS), propagation microbench 1M x 1,000",
+                "value": ev / dev_s, "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+                "warmup": warm, "ms_per_step": prof["step_ms"] / args.steps,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f32 weights, int32 fixed-point sums",
+                "data": "synthetic (seeded forced Poisson pre-spikes)",
+                "config": {"workload": f"propagation microbench, 1,000,000 LIF x fan-out 1,000 "
+                                       f"(1.0B synapses), rate {rate}, {mname}",
+                           "rate": rate, "mode": mname,
+                           "events_per_step": ev / args.steps,
+                           "post_spikes_per_step": (c1["total_spikes"] - c0["total_spikes"]) / args.steps,
+                           "ltp_visits_per_step": (c1["ltp_visits"] - c0["ltp_visits"]) / args.steps,
+                           "l2": "inputs larger than L2 (8 GB of synapse streams)"},
+                "e2e": {"value": e2e_ev / wall, "unit": UNIT, "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": net.words * 4},
+                "gpu_launches": int(sum(v["launches"] for v in prof["kernels"].values())),
+                "kernels_ms_per_step": {k: v["ms"] / max(v["launches"], 1)
+                                        for k, v in prof["kernels"].items()},
+                "roofline": {"bound": "hbm", "kernel": "k4_push", "achieved": achieved,
+                             "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                             "peak_kind": peak_kind, "bytes_per_launch": pb, "traffic": None},
+                "clocks": clk.summary(),
+            }
+            if cb:
+                line["cpu_baseline"] = cb
+            print(json.dumps(line), flush=True)
+            net.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -158,8 +264,14 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=1000)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="stage2e", choices=["stage2e", "prop"],
+                    help="stage2e: the 55k/10.7M network (one line); prop: the 1M x 1,000 "
+                         "propagation microbench (one line per mode and rate, 1 GPU)")
     args = ap.parse_args()
     warm = max(args.warmup, 3)
+    if args.workload == "prop":
+        prop_main(args)
+        return
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -66,6 +66,26 @@ extern "C" {
 /* ---- models and presets ---------------------------------------------- */
 #define SNN_MODEL_STAGE2E 0  /* AdEx + NMDA/Ca + STP + PSW STDP + delays   */
 #define SNN_MODEL_STAGE0 1   /* LIF + pair STDP + eligibility + dopamine   */
+#define SNN_MODEL_PROP 2     /* propagation microbench: forced Poisson pre-spikes,
+                                fixed fan-out, push propagation into LIF neurons */
+
+/* Propagation microbench modes (bit flags, SNN_MODEL_PROP only).  The model
+ * has no counterpart in the reference; its step t is:
+ *   1. pre-spikes: neuron i spikes iff hash(seed, t, i) < prop_rate * 2^32;
+ *      with SNN_PROP_STP its release is u*R of a per-neuron Tsodyks-Markram
+ *      state (U 0.5, tau_d 200, tau_f 50 steps), else 1;
+ *   2. push: acc[post] += round(w * release * 2^24) over the out-edges of
+ *      every spiking neuron (exact int32 sums); with SNN_PROP_STDP each
+ *      excitatory out-synapse then gets LTD -0.05*exp(-dt/20) scaled by
+ *      dopamine * w_max (dt = t - last LIF spike of its post);
+ *   3. LIF (Stage 0 form, threshold 1, refractory 2) on input acc * 2^-24;
+ *   4. with SNN_PROP_STDP: LTP +0.05*exp(-dt/20) * dopamine * w_max on the
+ *      excitatory incoming synapses of every LIF spike (dt = t - last
+ *      pre-spike before t), through a reverse CSR; weights clamp to
+ *      [0, w_max].  The first 80 % of neurons are excitatory. */
+#define SNN_PROP_PLAIN 0
+#define SNN_PROP_STDP 1
+#define SNN_PROP_STP 2
 
 #define SNN_PRESET_REF 0      /* constants exactly as the reference kernels */
 #define SNN_PRESET_BASELINE 1 /* constants as stated in the benchmark spec  */
@@ -79,7 +99,10 @@ typedef struct snn_config {
     int32_t e0;            /* Stage 2e E0 ablation (pure STDP)                 */
     int32_t phase_offset;  /* Stage 2e: added to the step for the phase table */
     int32_t raster_steps;  /* device spike-raster capacity in steps (0 = 1024) */
-    int32_t reserved[10];
+    int32_t prop_mode;     /* SNN_MODEL_PROP: SNN_PROP_* flags                 */
+    float prop_rate;       /* SNN_MODEL_PROP: forced spike probability per step */
+    float prop_w_max;      /* SNN_MODEL_PROP: weight bound (0 = 0.01 / (rate * fan-out)) */
+    int32_t reserved[7];
 } snn_config;
 
 /* Network construction by columns and layers.
@@ -88,7 +111,9 @@ typedef struct snn_config {
  *   reference rules (src/stage2e/network_init.cu:158-473) when rule == 0.
  * Stage 0: n_columns == 0 gives the single-block 2000/6000/2000 network; with
  *   n_columns > 0 each column is l4 (sensory) / l23 (association) / l5
- *   (motor) neurons. */
+ *   (motor) neurons.
+ * Propagation microbench: l4 neurons, deg_intra out-edges each (uniform
+ *   random targets, generated on the device from `seed`). */
 typedef struct snn_topology_spec {
     int32_t n_columns;
     int32_t l4, l23, l5, l6;
@@ -213,6 +238,27 @@ int snn_get_profile(snn_ctx* ctx, snn_profile* out);
 
 int snn_save(snn_ctx* ctx, const char* path, int32_t fmt);
 int snn_load(snn_ctx* ctx, const char* path, int32_t fmt);
+
+/* Push propagation of one step's spikes through a fixed-fan-out CSR held in
+ * device memory (replaces synaptic_transmission_kernel,
+ * src/cuda/synapse_kernel.cu:28-47, whose float atomicAdd order is not
+ * deterministic).  All pointers are device pointers; the call is
+ * asynchronous on `stream` (a cudaStream_t, NULL = legacy default stream):
+ *   for every neuron i < n_pre with spikes[i] != 0 and every k < fanout:
+ *     acc[post[i*fanout + k]] += rint(w[i*fanout + k] * 2^frac_bits)   (int32)
+ * The sum is exact integer arithmetic (wrapping on overflow), so the result
+ * does not depend on the order of the additions.  post[] entries must lie in
+ * [0, n_post) (others are skipped); |w| * 2^frac_bits < 2^31; 0 <= frac_bits
+ * <= 30.  The compacted list of spiking neurons lives in scratch device
+ * memory that the first call on a device allocates and later calls reuse
+ * (grown when n_pre grows; freed at process exit).  Calls on one device are
+ * chained on the device (each call's stream waits for the previous call), so
+ * calls from several streams or threads are safe but do not overlap; the call
+ * may allocate and must not be captured into a CUDA graph.  This is the push
+ * kernel of SNN_MODEL_PROP. */
+int snn_propagate(const int32_t* post, const float* w, int64_t n_pre, int32_t fanout,
+                  const uint8_t* spikes, int32_t* acc, int64_t n_post, int32_t frac_bits,
+                  void* stream);
 
 /* Seeded synthetic UTF-8 byte stream: a fraction p_cjk of characters are
  * CJK code points U+4E00..U+9FFF drawn Zipf(zipf_s) by rank (rank -> code

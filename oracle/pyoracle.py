@@ -286,3 +286,116 @@ class Oracle0:
             self.close()
         except Exception:
             pass
+
+
+# ---------------------------------------------------------------------------
+# Propagation microbench oracle (oracle/oracle4.cpp)
+# ---------------------------------------------------------------------------
+class O4Params(C.Structure):
+    _fields_ = [("n", C.c_int32), ("fanout", C.c_int32), ("seed", C.c_uint32),
+                ("mode", C.c_int32), ("rate", C.c_float), ("w_max", C.c_float),
+                ("dopamine", C.c_float), ("n_threads", C.c_int32)]
+
+
+class O4Counters(C.Structure):
+    _fields_ = [("step", C.c_int64), ("total_spikes", C.c_int64), ("events", C.c_int64),
+                ("pre_spikes", C.c_int64), ("ltp_visits", C.c_int64),
+                ("last_spikes", C.c_int32), ("n_exc", C.c_int32), ("n_synapses", C.c_int64)]
+
+
+def prop_w_max(rate, fanout):
+    """Default weight bound of the microbench: 0.01 / (rate * fan-out), as a
+    float32 (the value the engine derives when prop_w_max is 0)."""
+    if rate <= 0:
+        return 1.0
+    return float(np.float32(np.float32(0.01) / (np.float32(rate) * np.float32(fanout))))
+
+
+def prop_params(n=1_000_000, fanout=1000, seed=42, mode=0, rate=0.01, w_max=0.0,
+                dopamine=1.0, n_threads=0):
+    p = O4Params()
+    p.n, p.fanout, p.seed, p.mode, p.rate = n, fanout, seed, mode, rate
+    p.w_max = w_max if w_max > 0 else prop_w_max(rate, fanout)
+    p.dopamine, p.n_threads = dopamine, n_threads
+    return p
+
+
+class Oracle4:
+    FIELDS = {"V": (0, np.float32), "I": (1, np.float32), "u": (2, np.float32),
+              "R": (3, np.float32), "ref": (6, np.int32), "last_post": (7, np.int32),
+              "last_pre": (8, np.int32)}
+
+    def __init__(self, params):
+        L = lib()
+        if not hasattr(L, "_o4_ready"):
+            L.o4_create.restype = C.c_void_p
+            L.o4_create.argtypes = [C.POINTER(O4Params)]
+            L.o4_destroy.argtypes = [C.c_void_p]
+            L.o4_set_dopamine.argtypes = [C.c_void_p, C.c_float]
+            L.o4_run.argtypes = [C.c_void_p, C.c_int32, C.c_void_p]
+            L.o4_counters.argtypes = [C.c_void_p, C.POINTER(O4Counters)]
+            L.o4_get.argtypes = [C.c_void_p, C.c_int32, C.c_void_p]
+            L.o4_propagate.argtypes = [C.c_void_p, C.c_void_p, C.c_int64, C.c_int32,
+                                       C.c_void_p, C.c_void_p, C.c_int32]
+            L._o4_ready = True
+        self.L = L
+        self.P = params
+        self.h = L.o4_create(C.byref(params))
+        self.N = params.n
+        self.S = params.n * params.fanout
+
+    def run(self, n, raster=False):
+        r = np.zeros((n, (self.N + 31) // 32), np.uint32) if raster else None
+        self.L.o4_run(self.h, n, r.ctypes.data if r is not None else None)
+        return r
+
+    def counters(self):
+        c = O4Counters()
+        self.L.o4_counters(self.h, C.byref(c))
+        return {k: getattr(c, k) for k, _ in O4Counters._fields_}
+
+    def neuron(self, name):
+        idx, dt = self.FIELDS[name]
+        out = np.zeros(self.N, dt)
+        self.L.o4_get(self.h, idx, out.ctypes.data)
+        return out
+
+    def weights(self):
+        out = np.zeros(self.S, np.float32)
+        self.L.o4_get(self.h, 4, out.ctypes.data)
+        return out
+
+    def post(self):
+        out = np.zeros(self.S, np.int32)
+        self.L.o4_get(self.h, 5, out.ctypes.data)
+        return out
+
+    def set_dopamine(self, da):
+        self.L.o4_set_dopamine(self.h, da)
+
+    def close(self):
+        if self.h:
+            self.L.o4_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def propagate(post, w, fanout, spikes, n_post, frac_bits=24):
+    """Closed-form exact push (o4_propagate) of one spike vector."""
+    L = lib()
+    if not hasattr(L, "_o4_prop_ready"):
+        L.o4_propagate.argtypes = [C.c_void_p, C.c_void_p, C.c_int64, C.c_int32,
+                                   C.c_void_p, C.c_void_p, C.c_int32]
+        L._o4_prop_ready = True
+    post = np.ascontiguousarray(post, np.int32)
+    w = np.ascontiguousarray(w, np.float32)
+    spikes = np.ascontiguousarray(spikes, np.uint8)
+    acc = np.zeros(n_post, np.int32)
+    L.o4_propagate(post.ctypes.data, w.ctypes.data, len(spikes), fanout, spikes.ctypes.data,
+                   acc.ctypes.data, frac_bits)
+    return acc

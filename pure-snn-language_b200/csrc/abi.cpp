@@ -54,12 +54,14 @@ const char* snn_version(void) { return "snn_b200 0.1 (sm_100a)"; }
 
 int snn_config_init(snn_config* cfg, int32_t model, int32_t preset) {
     if (!cfg) return SNN_ERR_ARG;
-    if (model != SNN_MODEL_STAGE2E && model != SNN_MODEL_STAGE0) return SNN_ERR_ARG;
+    if (model != SNN_MODEL_STAGE2E && model != SNN_MODEL_STAGE0 && model != SNN_MODEL_PROP)
+        return SNN_ERR_ARG;
     if (preset != SNN_PRESET_REF && preset != SNN_PRESET_BASELINE) return SNN_ERR_ARG;
     memset(cfg, 0, sizeof(*cfg));
     cfg->model = model;
     cfg->preset = preset;
     cfg->raster_steps = 1024;
+    if (model == SNN_MODEL_PROP) cfg->prop_rate = 0.01f;
     return SNN_OK;
 }
 
@@ -85,6 +87,14 @@ int snn_topology_init(snn_topology_spec* spec, int32_t model, int32_t n_columns)
         spec->rule = 1;
         return SNN_OK;
     }
+    if (model == SNN_MODEL_PROP) {  // n_columns unused: 1M neurons, fan-out 1000
+        memset(spec, 0, sizeof(*spec));
+        spec->l4 = 1000000;
+        spec->deg_intra = 1000;
+        spec->seed = 42;
+        spec->rule = 1;
+        return SNN_OK;
+    }
     return SNN_ERR_ARG;
 }
 
@@ -103,6 +113,7 @@ int snn_create(const snn_config* cfg, snn_ctx** out) {
     int rc = guard(ctx, [&] {
         if (cfg->model == SNN_MODEL_STAGE2E) ctx->eng.reset(snnb::make_engine_stage2e(*cfg));
         else if (cfg->model == SNN_MODEL_STAGE0) ctx->eng.reset(snnb::make_engine_stage0(*cfg));
+        else if (cfg->model == SNN_MODEL_PROP) ctx->eng.reset(snnb::make_engine_prop(*cfg));
         else throw snnb::Error(SNN_ERR_ARG, "unknown model");
     });
     if (rc != SNN_OK) {
@@ -205,6 +216,22 @@ int snn_load(snn_ctx* ctx, const char* path, int32_t fmt) {
         SNN_REQUIRE(path, SNN_ERR_ARG, "null path");
         ctx->eng->load(path, fmt);
     });
+}
+
+int snn_propagate(const int32_t* post, const float* w, int64_t n_pre, int32_t fanout,
+                  const uint8_t* spikes, int32_t* acc, int64_t n_post, int32_t frac_bits,
+                  void* stream) {
+    try {
+        snnb::propagate(post, w, n_pre, fanout, spikes, acc, n_post, frac_bits, (cudaStream_t)stream);
+        g_create_err.clear();
+        return SNN_OK;
+    } catch (const snnb::Error& e) {
+        g_create_err = e.what();
+        return e.code;
+    } catch (const std::exception& e) {
+        g_create_err = e.what();
+        return SNN_ERR_STATE;
+    }
 }
 
 }  // extern "C"

@@ -1,0 +1,905 @@
+// engine_prop.cu - propagation microbench (SNN_MODEL_PROP) and the standalone
+// push entry point snn_propagate.
+//
+// One step t is three kernels (two without STDP), captured 50 steps per CUDA
+// graph:
+//   k4_push  warp-per-(spiking neuron, 512-synapse segment) push over the
+//            pre-major SoA streams int32 post[S] / f32 w[S]: 16-byte streaming
+//            loads, one int32 red.add per synapse into the L2-resident
+//            accumulator (exact, so order-free); LTD fused on the same
+//            registers (w rewritten with 16-byte streaming stores).
+//   k4_lif   thread per neuron: LIF on the accumulator (zeroing it), raster
+//            word by ballot, list of LIF spikes (STDP), and the forced spikes
+//            of step t+1 with their Tsodyks-Markram release (warp-aggregated
+//            appends to the double-buffered pre-spike list; step t+1's push
+//            commits the spike time and STP state).
+//   k4_ltp   warp per LIF spike: LTP over its incoming synapses through the
+//            reverse CSR (synapse ids), reading the pre's last spike before t.
+// The step index lives in device memory (t_base + the step's offset in the
+// graph), advanced by a one-thread kernel at the end of each launch.
+#include <algorithm>
+#include <mutex>
+#include "common.h"
+#include "snn_prop_rules.h"
+
+namespace {
+
+constexpr int P_THREADS = 256;
+constexpr int P_UNROLL = 4;                 // 16-byte vectors per lane per segment
+constexpr int P_SEG4 = 32 * P_UNROLL;       // vectors per segment (512 synapses)
+constexpr float Q_SCALE_INV = 5.9604644775390625e-8f;  // 2^-24
+
+struct PCtrl {
+    int t_base;
+    int learn;
+    float lr;                 // dopamine * w_max
+    int pad0;
+    unsigned n_pre[2];        // forced spikes of steps with parity 0 / 1
+    unsigned n_post;          // LIF spikes of the current step (STDP list)
+    unsigned pad1;
+    unsigned long long events, pre_spikes, post_spikes, ltp_visits;
+    long long raster_base;
+};
+
+struct PDev {
+    int N, F, n_exc, words, raster_cap;
+    uint32_t thr;
+    uint64_t key;
+    float w_max;
+    const int32_t* post;
+    float* w;
+    const uint32_t* in_ptr;
+    const uint32_t* rev;
+    int32_t* acc;
+    float *V, *I, *u, *R;
+    int8_t* ref;
+    int32_t *last_post, *tA, *tB;  // last / previous forced spike (committed by k4_push)
+    int32_t* pre_list;        // [2][N]
+    float *rel_list, *un_list, *rn_list;  // [2][N]: release and the STP state after it
+    int32_t* post_list;       // [N]
+    uint32_t* raster;
+    const float* exp_tab;
+    PCtrl* ctrl;
+};
+
+__device__ __forceinline__ float e20(const PDev& D, int dt) {
+    return dt <= SNN_PROP_EXP_STEPS ? __ldg(D.exp_tab + dt) : 0.0f;
+}
+
+// LTD of one excitatory out-synapse onto q (post spike strictly before t)
+__device__ __forceinline__ float ltd(const PDev& D, float w, int q, int t, float lr) {
+    const int lp = __ldcg(D.last_post + q);
+    if (lp < 0) return w;
+    const float dw = pm_mul(-0.05f, e20(D, t - lp));
+    return pm_min(pm_max(pm_fma(lr, dw, w), 0.0f), D.w_max);
+}
+
+// warp-aggregated append of flagged lanes to list[] (count at *cnt)
+__device__ __forceinline__ unsigned warp_append(bool flag, unsigned* cnt, int lane) {
+    const unsigned m = __ballot_sync(0xffffffffu, flag);
+    unsigned base = 0;
+    if (lane == 0 && m) base = atomicAdd(cnt, (unsigned)__popc(m));
+    base = __shfl_sync(0xffffffffu, base, 0);
+    return base + __popc(m & ((1u << lane) - 1u));
+}
+
+// forced spike of neuron j at step tn, appended to the pre-spike list of
+// parity tn & 1 with its STP release and the STP state after it; the state
+// and the spike time are committed by step tn's push, so that the exported
+// state always belongs to the last executed step.  All 32 lanes call it.
+template <bool STDP, bool STP>
+__device__ __forceinline__ void select_spike(const PDev& D, int tn, int j, int lane) {
+    bool ps = false;
+    float rel = 1.0f, uu = 0.0f, rr = 0.0f;
+    if (j < D.N) {
+        ps = snn_prop_spikes(D.key, tn, (uint32_t)j, D.thr);
+        if (ps && STP) {
+            const int a = D.tA[j];
+            uu = D.u[j];
+            rr = D.R[j];
+            rel = snn_prop_stp(&uu, &rr, a >= 0 ? tn - a : -1);
+        }
+    }
+    const unsigned pos = warp_append(ps, &D.ctrl->n_pre[tn & 1], lane);
+    if (ps) {
+        const size_t x = (size_t)(tn & 1) * D.N + pos;
+        D.pre_list[x] = j;
+        if (STP) {
+            D.rel_list[x] = rel;
+            D.un_list[x] = uu;
+            D.rn_list[x] = rr;
+        }
+    }
+}
+
+// step t's commit of spiker e (one writer: lane 0 of its first segment)
+template <bool STDP, bool STP>
+__device__ __forceinline__ void commit_spike(const PDev& D, int i, size_t x, int t) {
+    if (STDP) D.tB[i] = D.tA[i];
+    if (STDP || STP) D.tA[i] = t;
+    if (STP) {
+        D.u[i] = D.un_list[x];
+        D.R[i] = D.rn_list[x];
+    }
+}
+
+template <bool STDP, bool STP>
+__global__ void __launch_bounds__(P_THREADS) k4_select0(PDev D) {
+    const int j = blockIdx.x * P_THREADS + threadIdx.x;
+    select_spike<STDP, STP>(D, D.ctrl->t_base, j, threadIdx.x & 31);
+}
+
+template <bool STDP, bool STP>
+__global__ void __launch_bounds__(P_THREADS) k4_push(PDev D, int k) {
+    PCtrl* C = D.ctrl;
+    const int t = C->t_base + k;
+    const int par = t & 1;
+    const unsigned n = C->n_pre[par];
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        C->n_pre[par ^ 1] = 0;
+        C->n_post = 0;
+        C->events += (unsigned long long)n * (unsigned)D.F;
+        C->pre_spikes += n;
+    }
+    const int lane = threadIdx.x & 31;
+    const long long gw = ((long long)blockIdx.x * P_THREADS + threadIdx.x) >> 5;
+    const long long nw = ((long long)gridDim.x * P_THREADS) >> 5;
+    const int F4 = D.F >> 2;
+    const int nseg = (F4 + P_SEG4 - 1) / P_SEG4;
+    const long long items = (long long)n * nseg;
+    const int32_t* list = D.pre_list + (size_t)par * D.N;
+    const float* rl = D.rel_list + (size_t)par * D.N;
+    const bool learn = STDP && C->learn;
+    const float lr = C->lr;
+    for (long long it = gw; it < items; it += nw) {
+        const long long e = it / nseg;
+        const int c0 = (int)(it - e * nseg) * P_SEG4 + lane;
+        const int i = list[e];
+        const float rel = STP ? rl[e] : 1.0f;
+        if ((STDP || STP) && c0 == 0) commit_spike<STDP, STP>(D, i, (size_t)par * D.N + e, t);
+        const int4* p4 = reinterpret_cast<const int4*>(D.post) + (long long)i * F4;
+        float4* w4 = reinterpret_cast<float4*>(D.w) + (long long)i * F4;
+        int4 pv[P_UNROLL];
+        float4 wv[P_UNROLL];
+#pragma unroll
+        for (int u = 0; u < P_UNROLL; ++u) {
+            const int c = c0 + u * 32;
+            if (c < F4) {
+                pv[u] = __ldcs(p4 + c);
+                wv[u] = __ldcs(w4 + c);
+            }
+        }
+        const bool plastic = learn && i < D.n_exc;
+#pragma unroll
+        for (int u = 0; u < P_UNROLL; ++u) {
+            const int c = c0 + u * 32;
+            if (c < F4) {
+                atomicAdd(D.acc + pv[u].x, snn_prop_quant(wv[u].x, rel, STP));
+                atomicAdd(D.acc + pv[u].y, snn_prop_quant(wv[u].y, rel, STP));
+                atomicAdd(D.acc + pv[u].z, snn_prop_quant(wv[u].z, rel, STP));
+                atomicAdd(D.acc + pv[u].w, snn_prop_quant(wv[u].w, rel, STP));
+                if (plastic) {
+                    float4 nv;
+                    nv.x = ltd(D, wv[u].x, pv[u].x, t, lr);
+                    nv.y = ltd(D, wv[u].y, pv[u].y, t, lr);
+                    nv.z = ltd(D, wv[u].z, pv[u].z, t, lr);
+                    nv.w = ltd(D, wv[u].w, pv[u].w, t, lr);
+                    __stcs(w4 + c, nv);
+                }
+            }
+        }
+    }
+}
+
+// scalar form for fan-outs that are not a multiple of 4
+template <bool STDP, bool STP>
+__global__ void __launch_bounds__(P_THREADS) k4_push_scalar(PDev D, int k) {
+    PCtrl* C = D.ctrl;
+    const int t = C->t_base + k;
+    const int par = t & 1;
+    const unsigned n = C->n_pre[par];
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        C->n_pre[par ^ 1] = 0;
+        C->n_post = 0;
+        C->events += (unsigned long long)n * (unsigned)D.F;
+        C->pre_spikes += n;
+    }
+    const int lane = threadIdx.x & 31;
+    const long long gw = ((long long)blockIdx.x * P_THREADS + threadIdx.x) >> 5;
+    const long long nw = ((long long)gridDim.x * P_THREADS) >> 5;
+    const int nseg = (D.F + P_SEG4 - 1) / P_SEG4;
+    const long long items = (long long)n * nseg;
+    const int32_t* list = D.pre_list + (size_t)par * D.N;
+    const float* rl = D.rel_list + (size_t)par * D.N;
+    const bool learn = STDP && C->learn;
+    const float lr = C->lr;
+    for (long long it = gw; it < items; it += nw) {
+        const long long e = it / nseg;
+        const int c0 = (int)(it - e * nseg) * P_SEG4 + lane;
+        const int i = list[e];
+        const float rel = STP ? rl[e] : 1.0f;
+        if ((STDP || STP) && c0 == 0) commit_spike<STDP, STP>(D, i, (size_t)par * D.N + e, t);
+        const bool plastic = learn && i < D.n_exc;
+        const long long b = (long long)i * D.F;
+        for (int c = c0; c < D.F && c < c0 + P_SEG4; c += 32) {
+            const int q = __ldcs(D.post + b + c);
+            const float wv = __ldcs(D.w + b + c);
+            atomicAdd(D.acc + q, snn_prop_quant(wv, rel, STP));
+            if (plastic) __stcs(D.w + b + c, ltd(D, wv, q, t, lr));
+        }
+    }
+}
+
+template <bool STDP, bool STP>
+__global__ void __launch_bounds__(P_THREADS) k4_lif(PDev D, int k) {
+    PCtrl* C = D.ctrl;
+    const int t = C->t_base + k;
+    const int j = blockIdx.x * P_THREADS + threadIdx.x;
+    const int lane = threadIdx.x & 31;
+    bool sp = false;
+    if (j < D.N) {
+        const int a = __ldcg(D.acc + j);
+        D.acc[j] = 0;
+        const float in = pm_mul(pm_i2f(a), Q_SCALE_INV);
+        const int r = D.ref[j];
+        float v = D.V[j];
+        if (r > 0) {
+            D.ref[j] = (int8_t)(r - 1);
+            D.V[j] = pm_mul(v, 0.95f);
+        } else {
+            const float cur = pm_fma(D.I[j], 0.95f, in);
+            D.I[j] = cur;
+            v = pm_fma(v, 0.95f, cur);
+            if (v < 0.0f) v = 0.0f;
+            sp = v >= 1.0f;
+            if (sp) {
+                v = 0.0f;
+                D.ref[j] = 2;
+                D.last_post[j] = t;
+            }
+            D.V[j] = v;
+        }
+    }
+    const unsigned m = __ballot_sync(0xffffffffu, sp);
+    if (lane == 0 && (j >> 5) < D.words) {
+        const long long row = ((long long)t - C->raster_base) % D.raster_cap;
+        D.raster[row * D.words + (j >> 5)] = m;
+    }
+    __shared__ unsigned blk_spikes;
+    if (threadIdx.x == 0) blk_spikes = 0;
+    __syncthreads();
+    if (lane == 0 && m) atomicAdd(&blk_spikes, (unsigned)__popc(m));
+    if (STDP) {
+        const unsigned pos = warp_append(sp, &C->n_post, lane);
+        if (sp) D.post_list[pos] = j;
+    }
+    select_spike<STDP, STP>(D, t + 1, j, lane);
+    __syncthreads();
+    if (threadIdx.x == 0 && blk_spikes) atomicAdd(&C->post_spikes, (unsigned long long)blk_spikes);
+}
+
+// latest forced spike of p strictly before t (step t's push has committed
+// spikes up to t)
+__device__ __forceinline__ int pre_before(const PDev& D, int p, int t) {
+    const int a = __ldcg(D.tA + p);
+    return a < t ? a : __ldcg(D.tB + p);
+}
+
+__global__ void __launch_bounds__(P_THREADS) k4_ltp(PDev D, int k) {
+    PCtrl* C = D.ctrl;
+    if (!C->learn) return;
+    const int t = C->t_base + k;
+    const unsigned n = C->n_post;
+    const float lr = C->lr;
+    const int lane = threadIdx.x & 31;
+    const long long gw = ((long long)blockIdx.x * P_THREADS + threadIdx.x) >> 5;
+    const long long nw = ((long long)gridDim.x * P_THREADS) >> 5;
+    const uint32_t F = (uint32_t)D.F;
+    for (long long e = gw; e < (long long)n; e += nw) {
+        const int j = D.post_list[e];
+        const uint32_t b = D.in_ptr[j], en = D.in_ptr[j + 1];
+        if (lane == 0) atomicAdd(&C->ltp_visits, (unsigned long long)(en - b));
+        for (uint32_t x0 = b; x0 < en; x0 += 32 * P_UNROLL) {
+            uint32_t s[P_UNROLL];
+            int tp[P_UNROLL];
+#pragma unroll
+            for (int u = 0; u < P_UNROLL; ++u) {
+                const uint32_t x = x0 + u * 32 + lane;
+                s[u] = x < en ? __ldcs(D.rev + x) : 0xffffffffu;
+                tp[u] = -1;
+                if (s[u] != 0xffffffffu) {
+                    const int p = (int)(s[u] / F);
+                    if (p < D.n_exc) tp[u] = pre_before(D, p, t);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < P_UNROLL; ++u) {
+                if (tp[u] >= 0) {
+                    const float dw = pm_mul(0.05f, e20(D, t - tp[u]));
+                    const float wv = __ldcg(D.w + s[u]);
+                    D.w[s[u]] = pm_min(pm_max(pm_fma(lr, dw, wv), 0.0f), D.w_max);
+                }
+            }
+        }
+    }
+}
+
+__global__ void k4_advance(PCtrl* C, int n) { C->t_base += n; }
+
+// ---- build kernels ---------------------------------------------------------
+__global__ void k4_generate(int32_t* post, float* w, long long S, int N, int F, int n_exc,
+                            uint32_t seed, float w_max) {
+    for (long long s = (long long)blockIdx.x * blockDim.x + threadIdx.x; s < S;
+         s += (long long)gridDim.x * blockDim.x) {
+        const uint64_t h = snn_prop_syn_hash(seed, (uint64_t)s);
+        post[s] = snn_prop_post(h, (uint32_t)N);
+        w[s] = snn_prop_weight(h, w_max, (s / F) < n_exc);
+    }
+}
+
+__global__ void k4_indegree(const int32_t* post, long long S, uint32_t* deg) {
+    for (long long s = (long long)blockIdx.x * blockDim.x + threadIdx.x; s < S;
+         s += (long long)gridDim.x * blockDim.x)
+        atomicAdd(deg + post[s], 1u);
+}
+
+// exclusive scan of deg[0..N) into ptr[0..N] by one block of 1024 threads
+__global__ void __launch_bounds__(1024) k4_scan(const uint32_t* deg, uint32_t* ptr, int N) {
+    __shared__ unsigned long long part[1024];
+    const int tid = threadIdx.x;
+    const long long lo = (long long)N * tid / 1024, hi = (long long)N * (tid + 1) / 1024;
+    unsigned long long s = 0;
+    for (long long j = lo; j < hi; ++j) s += deg[j];
+    part[tid] = s;
+    __syncthreads();
+    for (int off = 1; off < 1024; off <<= 1) {
+        unsigned long long v = tid >= off ? part[tid - off] : 0;
+        __syncthreads();
+        part[tid] += v;
+        __syncthreads();
+    }
+    unsigned long long run = part[tid] - s;
+    for (long long j = lo; j < hi; ++j) {
+        ptr[j] = (uint32_t)run;
+        run += deg[j];
+    }
+    if (tid == 1023) ptr[N] = (uint32_t)part[1023];
+}
+
+__global__ void k4_fill_rev(const int32_t* post, long long S, uint32_t* cursor, uint32_t* rev) {
+    for (long long s = (long long)blockIdx.x * blockDim.x + threadIdx.x; s < S;
+         s += (long long)gridDim.x * blockDim.x)
+        rev[atomicAdd(cursor + post[s], 1u)] = (uint32_t)s;
+}
+
+__global__ void k4_exp_table(float* tab) {
+    const int k = blockIdx.x * blockDim.x + threadIdx.x;
+    if (k <= SNN_PROP_EXP_STEPS) tab[k] = snn_expf(pm_div(-pm_i2f(k), 20.0f));
+}
+
+__global__ void k4_max(const uint32_t* v, int n, uint32_t* out) {
+    uint32_t m = 0;
+    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < n; j += gridDim.x * blockDim.x)
+        m = max(m, v[j]);
+    for (int o = 16; o; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0 && m) atomicMax(out, m);
+}
+
+// ---- host engine -----------------------------------------------------------
+struct EngineProp : snnb::Engine {
+    snn_config cfg;
+    cudaStream_t stream = nullptr;
+    PDev D{};
+    int mode = 0;
+    bool stdp = false, stp = false, built = false, vec = false;
+    long long S = 0, steps = 0, raster_base_host = 0;
+    int raster_cap = 1024;
+    int push_grid = 1, lif_grid = 1, ltp_grid = 1;
+    uint32_t max_in = 0;
+    float dopamine = 1.0f;
+    snnb::DevBuf<int32_t> post, acc, last_post, tA, tB, pre_list, post_list;
+    snnb::DevBuf<float> w, V, I, u, R, rel_list, un_list, rn_list, exp_tab;
+    snnb::DevBuf<int8_t> ref;
+    snnb::DevBuf<uint32_t> in_ptr, rev, raster, tmp;
+    snnb::DevBuf<PCtrl> ctrl;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t graph_exec = nullptr;
+    int graph_steps = 0;
+    bool profiling = false;
+    std::vector<cudaEvent_t> pev;
+    snn_profile prof{};
+
+    explicit EngineProp(const snn_config& c) : cfg(c) {
+        mode = c.prop_mode;
+        SNN_REQUIRE(mode >= 0 && mode <= 3, SNN_ERR_ARG, "prop_mode must combine SNN_PROP_STDP / SNN_PROP_STP");
+        SNN_REQUIRE(c.prop_rate >= 0.0f && c.prop_rate <= 1.0f, SNN_ERR_ARG, "prop_rate must lie in [0, 1]");
+        stdp = mode & SNN_PROP_STDP;
+        stp = mode & SNN_PROP_STP;
+        if (c.raster_steps > 0) raster_cap = c.raster_steps;
+        SNN_CUDA(cudaSetDevice(c.device));
+        SNN_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+    }
+    ~EngineProp() override {
+        for (auto e : pev) cudaEventDestroy(e);
+        drop_graph();
+        if (stream) {
+            cudaStreamSynchronize(stream);
+            cudaStreamDestroy(stream);
+        }
+    }
+
+    void drop_graph() {
+        if (graph_exec) cudaGraphExecDestroy(graph_exec);
+        if (graph) cudaGraphDestroy(graph);
+        graph_exec = nullptr;
+        graph = nullptr;
+        graph_steps = 0;
+    }
+
+    int nkern() const { return stdp ? 3 : 2; }
+
+    void build(const snn_topology_spec& spec) override {
+        SNN_REQUIRE(!built, SNN_ERR_STATE, "network already built");
+        SNN_CUDA(cudaSetDevice(cfg.device));
+        const int N = spec.l4, F = spec.deg_intra;
+        SNN_REQUIRE(N >= 1 && F >= 1, SNN_ERR_ARG, "need l4 >= 1 neurons and deg_intra >= 1 out-edges");
+        S = (long long)N * F;
+        SNN_REQUIRE(S < (1ll << 32) - 1, SNN_ERR_ARG, "N * fan-out must stay below 2^32 - 1");
+        D.N = N;
+        D.F = F;
+        D.n_exc = (int)(((long long)N * 4) / 5);
+        D.words = (N + 31) / 32;
+        D.raster_cap = raster_cap;
+        const double th = (double)cfg.prop_rate * 4294967296.0;
+        D.thr = th >= 4294967295.0 ? 0xFFFFFFFFu : (uint32_t)th;
+        D.key = snn_prop_spike_key(spec.seed);
+        D.w_max = cfg.prop_w_max > 0.0f ? cfg.prop_w_max
+                  : (cfg.prop_rate > 0.0f ? pm_div(0.01f, pm_mul(cfg.prop_rate, (float)F)) : 1.0f);
+        SNN_REQUIRE(D.w_max <= 1.0f, SNN_ERR_ARG, "prop_w_max must be <= 1");
+        vec = (F % 4) == 0;
+
+        post.alloc(S);
+        w.alloc(S);
+        acc.alloc(N);
+        V.alloc(N);
+        I.alloc(N);
+        ref.alloc(N);
+        last_post.alloc(N);
+        pre_list.alloc((size_t)2 * N);
+        rel_list.alloc(stp ? (size_t)2 * N : 1);
+        un_list.alloc(stp ? (size_t)2 * N : 1);
+        rn_list.alloc(stp ? (size_t)2 * N : 1);
+        raster.alloc((size_t)raster_cap * D.words);
+        exp_tab.alloc(SNN_PROP_EXP_STEPS + 1);
+        ctrl.alloc(1);
+        tmp.alloc((size_t)N + 1);
+        const int gen_grid = 148 * 16;
+        k4_generate<<<gen_grid, 256, 0, stream>>>(post.p, w.p, S, N, F, D.n_exc, spec.seed, D.w_max);
+        k4_exp_table<<<(SNN_PROP_EXP_STEPS + 256) / 256, 256, 0, stream>>>(exp_tab.p);
+        // in-degrees: the int32 accumulator must hold max in-degree * w_max * 2^24
+        tmp.zero(stream);
+        k4_indegree<<<gen_grid, 256, 0, stream>>>(post.p, S, tmp.p);
+        snnb::DevBuf<uint32_t> mx;
+        mx.alloc(1);
+        mx.zero(stream);
+        k4_max<<<148, 256, 0, stream>>>(tmp.p, N, mx.p);
+        SNN_CUDA(cudaMemcpyAsync(&max_in, mx.p, 4, cudaMemcpyDeviceToHost, stream));
+        SNN_CUDA(cudaStreamSynchronize(stream));
+        SNN_REQUIRE((double)max_in * D.w_max * 16777216.0 < 2147483647.0, SNN_ERR_ARG,
+                    "max in-degree * w_max * 2^24 overflows the int32 accumulator");
+        if (stdp) {
+            in_ptr.alloc((size_t)N + 1);
+            rev.alloc(S);
+            k4_scan<<<1, 1024, 0, stream>>>(tmp.p, in_ptr.p, N);
+            SNN_CUDA(cudaMemcpyAsync(tmp.p, in_ptr.p, (size_t)N * 4, cudaMemcpyDeviceToDevice, stream));
+            k4_fill_rev<<<gen_grid, 256, 0, stream>>>(post.p, S, tmp.p, rev.p);
+            post_list.alloc(N);
+            tA.alloc(N); tB.alloc(N);
+        } else if (stp) {
+            tA.alloc(N);
+        }
+        tmp.release();
+        if (stp) {
+            u.alloc(N);
+            R.alloc(N);
+        }
+        D.post = post.p; D.w = w.p; D.in_ptr = in_ptr.p; D.rev = rev.p; D.acc = acc.p;
+        D.V = V.p; D.I = I.p; D.u = u.p; D.R = R.p; D.ref = ref.p; D.last_post = last_post.p;
+        D.tA = tA.p; D.tB = tB.p; D.pre_list = pre_list.p; D.rel_list = rel_list.p;
+        D.un_list = un_list.p; D.rn_list = rn_list.p;
+        D.post_list = post_list.p; D.raster = raster.p; D.exp_tab = exp_tab.p; D.ctrl = ctrl.p;
+        reset_state();
+        int dev_sms = 0, occ = 0;
+        SNN_CUDA(cudaDeviceGetAttribute(&dev_sms, cudaDevAttrMultiProcessorCount, cfg.device));
+        if (vec) SNN_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, push_kernel(), P_THREADS, 0));
+        else SNN_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, push_kernel_scalar(), P_THREADS, 0));
+        push_grid = dev_sms * std::max(occ, 1);
+        lif_grid = (N + P_THREADS - 1) / P_THREADS;
+        ltp_grid = dev_sms * 8;
+        built = true;
+    }
+
+    void (*push_kernel())(PDev, int) {
+        if (stdp) return stp ? k4_push<true, true> : k4_push<true, false>;
+        return stp ? k4_push<false, true> : k4_push<false, false>;
+    }
+    void (*push_kernel_scalar())(PDev, int) {
+        if (stdp) return stp ? k4_push_scalar<true, true> : k4_push_scalar<true, false>;
+        return stp ? k4_push_scalar<false, true> : k4_push_scalar<false, false>;
+    }
+    void (*lif_kernel())(PDev, int) {
+        if (stdp) return stp ? k4_lif<true, true> : k4_lif<true, false>;
+        return stp ? k4_lif<false, true> : k4_lif<false, false>;
+    }
+
+    void reset_state() {
+        const int N = D.N;
+        acc.zero(stream);
+        V.zero(stream);
+        I.zero(stream);
+        ref.zero(stream);
+        SNN_CUDA(cudaMemsetAsync(last_post.p, 0xff, (size_t)N * 4, stream));  // -1: none
+        if (tA.p) SNN_CUDA(cudaMemsetAsync(tA.p, 0xff, (size_t)N * 4, stream));
+        if (tB.p) SNN_CUDA(cudaMemsetAsync(tB.p, 0xff, (size_t)N * 4, stream));
+        if (stp) {
+            std::vector<float> hu((size_t)N, SNN_PROP_STP_U), hr((size_t)N, 1.0f);
+            u.upload(hu.data(), N, stream);
+            R.upload(hr.data(), N, stream);
+            SNN_CUDA(cudaStreamSynchronize(stream));
+        }
+        raster.zero(stream);
+        PCtrl h{};
+        h.learn = 1;
+        h.lr = pm_mul(dopamine, D.w_max);
+        ctrl.upload(&h, 1, stream);
+        // forced spikes of step 0
+        if (stdp) {
+            if (stp) k4_select0<true, true><<<lif_blocks(), P_THREADS, 0, stream>>>(D);
+            else k4_select0<true, false><<<lif_blocks(), P_THREADS, 0, stream>>>(D);
+        } else {
+            if (stp) k4_select0<false, true><<<lif_blocks(), P_THREADS, 0, stream>>>(D);
+            else k4_select0<false, false><<<lif_blocks(), P_THREADS, 0, stream>>>(D);
+        }
+        SNN_CUDA(cudaGetLastError());
+        SNN_CUDA(cudaStreamSynchronize(stream));
+    }
+    int lif_blocks() const { return (D.N + P_THREADS - 1) / P_THREADS; }
+
+    void launch_step(int k, cudaEvent_t* ev, bool capturing) {
+        const unsigned fl = capturing ? cudaEventRecordExternal : cudaEventRecordDefault;
+        if (ev) SNN_CUDA(cudaEventRecordWithFlags(ev[0], stream, fl));
+        if (vec) push_kernel()<<<push_grid, P_THREADS, 0, stream>>>(D, k);
+        else push_kernel_scalar()<<<push_grid, P_THREADS, 0, stream>>>(D, k);
+        if (ev) SNN_CUDA(cudaEventRecordWithFlags(ev[1], stream, fl));
+        lif_kernel()<<<lif_grid, P_THREADS, 0, stream>>>(D, k);
+        if (ev) SNN_CUDA(cudaEventRecordWithFlags(ev[2], stream, fl));
+        if (stdp) {
+            k4_ltp<<<ltp_grid, P_THREADS, 0, stream>>>(D, k);
+            if (ev) SNN_CUDA(cudaEventRecordWithFlags(ev[3], stream, fl));
+        }
+    }
+
+    void ensure_events(int n) {
+        const size_t need = (size_t)n * (nkern() + 1);
+        while (pev.size() < need) {
+            cudaEvent_t e;
+            SNN_CUDA(cudaEventCreate(&e));
+            pev.push_back(e);
+        }
+    }
+    cudaEvent_t* step_events(int q) { return profiling ? &pev[(size_t)q * (nkern() + 1)] : nullptr; }
+
+    void ensure_graph(int n) {
+        if (graph_exec && graph_steps == n) return;
+        drop_graph();
+        if (profiling) ensure_events(n);
+        SNN_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+        for (int q = 0; q < n; ++q) launch_step(q, step_events(q), true);
+        k4_advance<<<1, 1, 0, stream>>>(ctrl.p, n);
+        SNN_CUDA(cudaStreamEndCapture(stream, &graph));
+        SNN_CUDA(cudaGraphInstantiate(&graph_exec, graph, 0));
+        graph_steps = n;
+    }
+
+    void harvest(int n) {
+        SNN_CUDA(cudaStreamSynchronize(stream));
+        const int nk = nkern();
+        for (int q = 0; q < n; ++q)
+            for (int kk = 0; kk < nk; ++kk) {
+                float ms = 0.0f;
+                cudaEvent_t* ev = step_events(q);
+                SNN_CUDA(cudaEventElapsedTime(&ms, ev[kk], ev[kk + 1]));
+                prof.kernel_ms[kk] += ms;
+                prof.launches[kk] += 1;
+                prof.step_ms += ms;
+            }
+        prof.steps += n;
+    }
+
+    void set_profiling(int32_t en) override {
+        SNN_REQUIRE(built, SNN_ERR_STATE, "build the network first");
+        SNN_CUDA(cudaStreamSynchronize(stream));
+        profiling = en != 0;
+        drop_graph();
+        memset(&prof, 0, sizeof(prof));
+        prof.n_kernels = nkern();
+        strcpy(prof.names[0], vec ? "k4_push" : "k4_push_scalar");
+        strcpy(prof.names[1], "k4_lif");
+        if (stdp) strcpy(prof.names[2], "k4_ltp");
+    }
+    void get_profile(snn_profile* o) override { *o = prof; }
+
+    void set_corpus(const uint8_t*, int64_t) override {}  // the input is the forced spikes
+
+    void run(int32_t n_steps, int32_t byte_override, int32_t learn, uint32_t* raster_out,
+             int32_t* counts_out) override {
+        SNN_REQUIRE(built, SNN_ERR_STATE, "build the network first");
+        SNN_REQUIRE(n_steps >= 0, SNN_ERR_ARG, "negative step count");
+        (void)byte_override;
+        if (n_steps == 0) return;
+        const int lr = learn ? 1 : 0;
+        SNN_CUDA(cudaMemcpyAsync((char*)ctrl.p + offsetof(PCtrl, learn), &lr, 4, cudaMemcpyHostToDevice, stream));
+        const long long rb = steps;
+        raster_base_host = rb;
+        SNN_CUDA(cudaMemcpyAsync((char*)ctrl.p + offsetof(PCtrl, raster_base), &rb, 8, cudaMemcpyHostToDevice, stream));
+        const int chunk = 50;
+        int done = 0;
+        while (done < n_steps) {
+            const int span = std::min(n_steps - done, raster_cap - (done % raster_cap));
+            int q = 0;
+            while (q < span) {
+                const int m = span - q >= chunk ? chunk : 1;
+                if (m == chunk) {
+                    ensure_graph(chunk);
+                    SNN_CUDA(cudaGraphLaunch(graph_exec, stream));
+                } else {
+                    if (profiling) ensure_events(1);
+                    launch_step(0, step_events(0), false);
+                    k4_advance<<<1, 1, 0, stream>>>(ctrl.p, 1);
+                    SNN_CUDA(cudaGetLastError());
+                }
+                if (profiling) harvest(m);
+                q += m;
+            }
+            if (raster_out || counts_out) {
+                const long long row0 = done % raster_cap;
+                std::vector<uint32_t> tmpr;
+                uint32_t* dst = raster_out ? raster_out + (size_t)done * D.words : nullptr;
+                if (!dst) {
+                    tmpr.resize((size_t)span * D.words);
+                    dst = tmpr.data();
+                }
+                SNN_CUDA(cudaMemcpyAsync(dst, raster.p + row0 * D.words, (size_t)span * D.words * 4,
+                                         cudaMemcpyDeviceToHost, stream));
+                SNN_CUDA(cudaStreamSynchronize(stream));
+                if (counts_out)
+                    for (int r = 0; r < span; ++r) {
+                        int cnt = 0;
+                        for (int x = 0; x < D.words; ++x) cnt += __builtin_popcount(dst[(size_t)r * D.words + x]);
+                        counts_out[done + r] = cnt;
+                    }
+            }
+            done += span;
+        }
+        steps += n_steps;
+        SNN_CUDA(cudaGetLastError());
+    }
+
+    void sync() override { SNN_CUDA(cudaStreamSynchronize(stream)); }
+    int64_t steps_done() const override { return steps; }
+
+    void counters(snn_counters* o) override {
+        SNN_REQUIRE(built, SNN_ERR_STATE, "build the network first");
+        PCtrl h;
+        SNN_CUDA(cudaMemcpyAsync(&h, ctrl.p, sizeof(PCtrl), cudaMemcpyDeviceToHost, stream));
+        SNN_CUDA(cudaStreamSynchronize(stream));
+        memset(o, 0, sizeof(*o));
+        o->step = steps;
+        o->total_spikes = (int64_t)h.post_spikes;
+        o->arrivals = (int64_t)h.events;
+        o->dispatched = (int64_t)h.pre_spikes;
+        o->ltp_visits = (int64_t)h.ltp_visits;
+        o->n_neurons = D.N;
+        o->n_synapses = S;
+        o->last_byte = -1;
+        if (steps > 0) {
+            std::vector<uint32_t> row(D.words);
+            get_spikes(row.data(), D.words);
+            int c = 0;
+            for (uint32_t x : row) c += __builtin_popcount(x);
+            o->last_spikes = c;
+        }
+        o->modeled_bytes = (double)h.events * 8.0 + (double)h.pre_spikes * 4.0 +
+                           (double)steps * D.N * 22.0;
+    }
+
+    void get_spikes(uint32_t* words, int64_t n_words) override {
+        SNN_REQUIRE(built && steps > 0, SNN_ERR_STATE, "no step executed yet");
+        SNN_REQUIRE(n_words >= D.words, SNN_ERR_ARG, "bitmask buffer too small");
+        const long long row = (steps - 1 - raster_base_host) % raster_cap;
+        SNN_CUDA(cudaMemcpyAsync(words, raster.p + row * D.words, (size_t)D.words * 4,
+                                 cudaMemcpyDeviceToHost, stream));
+        SNN_CUDA(cudaStreamSynchronize(stream));
+    }
+
+    void get_state(int32_t which, void* buf, int64_t nbytes) override {
+        SNN_REQUIRE(built, SNN_ERR_STATE, "build the network first");
+        const int64_t N = D.N;
+        auto need = [&](int64_t b) { SNN_REQUIRE(nbytes >= b, SNN_ERR_ARG, "state buffer too small"); };
+        auto dl = [&](const void* src, size_t b) {
+            need((int64_t)b);
+            SNN_CUDA(cudaMemcpyAsync(buf, src, b, cudaMemcpyDeviceToHost, stream));
+            SNN_CUDA(cudaStreamSynchronize(stream));
+        };
+        switch (which) {
+            case SNN_STATE_V: dl(V.p, N * 4); break;
+            case SNN_STATE_SYN_CURRENT: dl(I.p, N * 4); break;
+            case SNN_STATE_LAST_SPIKE: dl(last_post.p, N * 4); break;
+            case SNN_STATE_REFRACTORY: {
+                need(N * 4);
+                std::vector<int8_t> h((size_t)N);
+                SNN_CUDA(cudaMemcpyAsync(h.data(), ref.p, (size_t)N, cudaMemcpyDeviceToHost, stream));
+                SNN_CUDA(cudaStreamSynchronize(stream));
+                for (int64_t j = 0; j < N; ++j) ((int32_t*)buf)[j] = h[j];
+                break;
+            }
+            case SNN_STATE_WEIGHT: dl(w.p, S * 4); break;
+            case SNN_STATE_POST: dl(post.p, S * 4); break;
+            case SNN_STATE_RESOURCE:
+                SNN_REQUIRE(stp, SNN_ERR_UNSUPPORTED, "STP state exists only with SNN_PROP_STP");
+                dl(R.p, N * 4);
+                break;
+            case SNN_STATE_UTIL:
+                SNN_REQUIRE(stp, SNN_ERR_UNSUPPORTED, "STP state exists only with SNN_PROP_STP");
+                dl(u.p, N * 4);
+                break;
+            case SNN_STATE_ROW_PTR:
+                SNN_REQUIRE(stdp, SNN_ERR_UNSUPPORTED, "the reverse CSR exists only with SNN_PROP_STDP");
+                dl(in_ptr.p, (N + 1) * 4);
+                break;
+            default: throw snnb::Error(SNN_ERR_UNSUPPORTED, "state field not available in this model");
+        }
+    }
+
+    void set_dopamine(float da) override {
+        SNN_REQUIRE(built, SNN_ERR_STATE, "build the network first");
+        dopamine = da;
+        const float lr = pm_mul(da, D.w_max);
+        SNN_CUDA(cudaMemcpyAsync((char*)ctrl.p + offsetof(PCtrl, lr), &lr, 4, cudaMemcpyHostToDevice, stream));
+        SNN_CUDA(cudaStreamSynchronize(stream));
+    }
+
+    void save(const char*, int32_t) override {
+        throw snnb::Error(SNN_ERR_UNSUPPORTED, "the propagation microbench has no checkpoint format");
+    }
+    void load(const char*, int32_t) override {
+        throw snnb::Error(SNN_ERR_UNSUPPORTED, "the propagation microbench has no checkpoint format");
+    }
+};
+
+// ---- snn_propagate ----------------------------------------------------------
+__global__ void __launch_bounds__(P_THREADS) k_compact(const uint8_t* spikes, long long n,
+                                                        int32_t* list, unsigned* count) {
+    const int lane = threadIdx.x & 31;
+    for (long long i0 = (long long)blockIdx.x * P_THREADS; i0 < n; i0 += (long long)gridDim.x * P_THREADS) {
+        const long long i = i0 + threadIdx.x;
+        const bool f = i < n && spikes[i] != 0;
+        const unsigned pos = warp_append(f, count, lane);
+        if (f && pos < (unsigned long long)n) list[pos] = (int32_t)i;
+    }
+}
+
+// post indices outside [0, n_post) are skipped (the caller's arrays are not
+// trusted to be in range)
+__device__ __forceinline__ void add_checked(int32_t* acc, int n_post, int q, float w, float scale) {
+    if ((unsigned)q < (unsigned)n_post) atomicAdd(acc + q, (int32_t)pm_rint(pm_mul(w, scale)));
+}
+
+template <bool VEC>
+__global__ void __launch_bounds__(P_THREADS) k_push_fixed(const int32_t* post, const float* w, int F,
+                                                          const int32_t* list, const unsigned* count,
+                                                          int32_t* acc, int n_post, float scale) {
+    const unsigned n = *count;
+    const int lane = threadIdx.x & 31;
+    const long long gw = ((long long)blockIdx.x * P_THREADS + threadIdx.x) >> 5;
+    const long long nw = ((long long)gridDim.x * P_THREADS) >> 5;
+    const int F4 = VEC ? F >> 2 : F;
+    const int nseg = (F4 + P_SEG4 - 1) / P_SEG4;
+    const long long items = (long long)n * nseg;
+    for (long long it = gw; it < items; it += nw) {
+        const long long e = it / nseg;
+        const int c0 = (int)(it - e * nseg) * P_SEG4 + lane;
+        const long long i = list[e];
+        if (VEC) {
+            const int4* p4 = reinterpret_cast<const int4*>(post) + i * F4;
+            const float4* w4 = reinterpret_cast<const float4*>(w) + i * F4;
+            int4 pv[P_UNROLL];
+            float4 wv[P_UNROLL];
+#pragma unroll
+            for (int u = 0; u < P_UNROLL; ++u) {
+                const int c = c0 + u * 32;
+                if (c < F4) {
+                    pv[u] = __ldcs(p4 + c);
+                    wv[u] = __ldcs(w4 + c);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < P_UNROLL; ++u) {
+                const int c = c0 + u * 32;
+                if (c < F4) {
+                    add_checked(acc, n_post, pv[u].x, wv[u].x, scale);
+                    add_checked(acc, n_post, pv[u].y, wv[u].y, scale);
+                    add_checked(acc, n_post, pv[u].z, wv[u].z, scale);
+                    add_checked(acc, n_post, pv[u].w, wv[u].w, scale);
+                }
+            }
+        } else {
+            const long long b = i * F;
+            for (int c = c0; c < F && c < c0 + P_SEG4; c += 32)
+                add_checked(acc, n_post, __ldcs(post + b + c), __ldcs(w + b + c), scale);
+        }
+    }
+}
+
+// per-device scratch of snn_propagate: compacted spike list + its count.
+// Calls are chained on the device through `done` (each call's stream waits
+// for the previous call), so two calls never use the scratch at once even
+// when they are issued on different streams.
+struct PropScratch {
+    std::mutex mu;
+    int32_t* list = nullptr;
+    unsigned* count = nullptr;
+    long long cap = 0;
+    int sms = 0;
+    cudaEvent_t done = nullptr;
+    bool recorded = false;
+    ~PropScratch() {
+        if (list) cudaFree(list);
+        if (count) cudaFree(count);
+        if (done) cudaEventDestroy(done);
+    }
+};
+PropScratch g_scratch[64];
+
+}  // namespace
+
+namespace snnb {
+Engine* make_engine_prop(const snn_config& cfg) { return new EngineProp(cfg); }
+
+void propagate(const int32_t* post, const float* w, int64_t n_pre, int32_t fanout, const uint8_t* spikes,
+               int32_t* acc, int64_t n_post, int32_t frac_bits, cudaStream_t st) {
+    SNN_REQUIRE(post && w && spikes && acc, SNN_ERR_ARG, "null device pointer");
+    SNN_REQUIRE(n_pre >= 0 && n_pre < (1ll << 31), SNN_ERR_ARG, "n_pre must lie in [0, 2^31)");
+    SNN_REQUIRE(fanout >= 1, SNN_ERR_ARG, "fanout must be >= 1");
+    SNN_REQUIRE(n_post >= 1 && n_post < (1ll << 31), SNN_ERR_ARG, "n_post must lie in [1, 2^31)");
+    SNN_REQUIRE(frac_bits >= 0 && frac_bits <= 30, SNN_ERR_ARG, "frac_bits must lie in [0, 30]");
+    if (n_pre == 0) return;
+    int dev = 0;
+    SNN_CUDA(cudaGetDevice(&dev));
+    SNN_REQUIRE(dev >= 0 && dev < 64, SNN_ERR_ARG, "device ordinal above 63");
+    PropScratch& sc = g_scratch[dev];
+    std::lock_guard<std::mutex> lk(sc.mu);
+    if (!sc.done) SNN_CUDA(cudaEventCreateWithFlags(&sc.done, cudaEventDisableTiming));
+    if (sc.cap < n_pre) {
+        if (sc.recorded) SNN_CUDA(cudaEventSynchronize(sc.done));  // the old list may still be read
+        if (sc.list) cudaFree(sc.list);
+        sc.list = nullptr;
+        sc.cap = 0;
+        SNN_CUDA(cudaMalloc((void**)&sc.list, (size_t)n_pre * 4));
+        sc.cap = n_pre;
+    }
+    if (!sc.count) SNN_CUDA(cudaMalloc((void**)&sc.count, 4));
+    if (!sc.sms) SNN_CUDA(cudaDeviceGetAttribute(&sc.sms, cudaDevAttrMultiProcessorCount, dev));
+    if (sc.recorded) SNN_CUDA(cudaStreamWaitEvent(st, sc.done, 0));
+    SNN_CUDA(cudaMemsetAsync(sc.count, 0, 4, st));
+    const long long cb = std::min<long long>((n_pre + P_THREADS - 1) / P_THREADS, (long long)sc.sms * 8);
+    k_compact<<<(unsigned)cb, P_THREADS, 0, st>>>(spikes, n_pre, sc.list, sc.count);
+    const float scale = pm_bits2f((uint32_t)(127 + frac_bits) << 23);
+    const bool vec = (fanout % 4) == 0 && ((uintptr_t)post % 16) == 0 && ((uintptr_t)w % 16) == 0;
+    if (vec) k_push_fixed<true><<<sc.sms * 8, P_THREADS, 0, st>>>(post, w, fanout, sc.list, sc.count, acc, (int)n_post, scale);
+    else k_push_fixed<false><<<sc.sms * 8, P_THREADS, 0, st>>>(post, w, fanout, sc.list, sc.count, acc, (int)n_post, scale);
+    SNN_CUDA(cudaGetLastError());
+    SNN_CUDA(cudaEventRecord(sc.done, st));
+    sc.recorded = true;
+}
+}  // namespace snnb

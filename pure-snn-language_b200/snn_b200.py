@@ -22,7 +22,8 @@ LIB_PATH = os.path.join(HERE, "libsnn_b200.so")
 SNN_OK = 0
 ERRORS = {1: "SNN_ERR_ARG", 2: "SNN_ERR_CUDA", 3: "SNN_ERR_OOM", 4: "SNN_ERR_STATE",
           5: "SNN_ERR_IO", 6: "SNN_ERR_UNSUPPORTED", 7: "SNN_ERR_NO_DEVICE"}
-MODEL_STAGE2E, MODEL_STAGE0 = 0, 1
+MODEL_STAGE2E, MODEL_STAGE0, MODEL_PROP = 0, 1, 2
+PROP_PLAIN, PROP_STDP, PROP_STP = 0, 1, 2
 PRESET_REF, PRESET_BASELINE = 0, 1
 FMT_NATIVE, FMT_SNN2_V1, FMT_SCKP_V2, FMT_RAW_F32 = 0, 1, 2, 3
 
@@ -54,7 +55,8 @@ class SnnError(RuntimeError):
 class Config(C.Structure):
     _fields_ = [("model", C.c_int32), ("preset", C.c_int32), ("device", C.c_int32),
                 ("e0", C.c_int32), ("phase_offset", C.c_int32), ("raster_steps", C.c_int32),
-                ("reserved", C.c_int32 * 10)]
+                ("prop_mode", C.c_int32), ("prop_rate", C.c_float), ("prop_w_max", C.c_float),
+                ("reserved", C.c_int32 * 7)]
 
 
 class TopologySpec(C.Structure):
@@ -95,7 +97,7 @@ EXPORTS = ["snn_config_init", "snn_topology_init", "snn_create", "snn_destroy",
            "snn_last_error", "snn_version", "snn_build_columns", "snn_set_corpus", "snn_step",
            "snn_run", "snn_synchronize", "snn_get_spikes", "snn_get_state", "snn_get_counters",
            "snn_set_dopamine", "snn_set_e0", "snn_save", "snn_load", "snn_stream_generate",
-           "snn_set_profiling", "snn_get_profile"]
+           "snn_set_profiling", "snn_get_profile", "snn_propagate"]
 
 _lib = None
 
@@ -131,8 +133,25 @@ def lib():
         L.snn_stream_generate.argtypes = [vp, C.c_int64, C.c_uint64, C.c_double, C.c_double]
         L.snn_set_profiling.argtypes = [vp, C.c_int32]
         L.snn_get_profile.argtypes = [vp, C.POINTER(Profile)]
+        L.snn_propagate.argtypes = [vp, vp, C.c_int64, C.c_int32, vp, vp, C.c_int64, C.c_int32, vp]
         _lib = L
     return _lib
+
+
+def propagate(post, w, fanout, spikes, acc, frac_bits=24, stream=None):
+    """snn_propagate on torch CUDA tensors (int32 post[n_pre*fanout],
+    float32 w[...], uint8 spikes[n_pre], int32 acc[n_post], accumulated in
+    place) on `stream` (a torch.cuda.Stream, default: the current stream)."""
+    import torch
+    for t_, dt in ((post, torch.int32), (w, torch.float32), (spikes, torch.uint8), (acc, torch.int32)):
+        if not (t_.is_cuda and t_.dtype == dt and t_.is_contiguous()):
+            raise SnnError(1, "propagate wants contiguous CUDA tensors int32/float32/uint8/int32")
+    st = stream if stream is not None else torch.cuda.current_stream(acc.device)
+    rc = lib().snn_propagate(post.data_ptr(), w.data_ptr(), spikes.numel(), fanout,
+                             spikes.data_ptr(), acc.data_ptr(), acc.numel(), frac_bits,
+                             st.cuda_stream)
+    if rc:
+        raise SnnError(rc, lib().snn_last_error(None).decode())
 
 
 def stream(n, seed=42, p_cjk=0.452, zipf_s=1.1):
@@ -168,12 +187,14 @@ class Network:
     """One network on one GPU (one snn_ctx)."""
 
     def __init__(self, model=MODEL_STAGE2E, preset=PRESET_REF, device=0, e0=False,
-                 phase_offset=0, raster_steps=1024):
+                 phase_offset=0, raster_steps=1024, prop_mode=0, prop_rate=0.01, prop_w_max=0.0):
         L = lib()
         self.L = L
         cfg = Config()
         self._check(L.snn_config_init(C.byref(cfg), model, preset), None)
         cfg.device, cfg.e0, cfg.phase_offset, cfg.raster_steps = device, int(e0), phase_offset, raster_steps
+        if model == MODEL_PROP:
+            cfg.prop_mode, cfg.prop_rate, cfg.prop_w_max = prop_mode, prop_rate, prop_w_max
         h = C.c_void_p()
         rc = L.snn_create(C.byref(cfg), C.byref(h))
         if rc:
@@ -243,6 +264,8 @@ class Network:
 
     def state(self, name):
         which, dt, shape = STATE[name]
+        if self.model == MODEL_PROP and name in ("R", "u"):
+            shape = "N"  # per pre-synaptic neuron in the microbench
         n = {"N": self.N, "S": self.S, "N1": self.N + 1, "4": 4, "256": 256,
              "N256": self.N * 256, "G4": 4 * self.n_columns}[shape]
         out = np.zeros(n, dt)

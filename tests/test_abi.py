@@ -18,7 +18,7 @@ def declared_functions():
     names = set()
     inc = os.path.join(ROOT, "include")
     for fn in os.listdir(inc):
-        if not fn.endswith(".h") or fn == "snn_pmath.h":
+        if not fn.endswith(".h") or fn in ("snn_pmath.h", "snn_prop_rules.h"):  # inline helpers
             continue
         txt = open(os.path.join(inc, fn)).read()
         txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
