@@ -260,6 +260,23 @@ int snn_propagate(const int32_t* post, const float* w, int64_t n_pre, int32_t fa
                   const uint8_t* spikes, int32_t* acc, int64_t n_post, int32_t frac_bits,
                   void* stream);
 
+/* snn_propagate without any allocation (no counterpart in the reference).
+ * For callers that must not allocate device memory once they run: cudaMalloc
+ * and cudaFree synchronise the whole device, which stalls a pipelined
+ * multi-stream simulation loop, and a process that reserves its device
+ * memory up front (a fixed budget, or a pool that owns the rest of the GPU)
+ * has nothing left to grant.  Same arguments, semantics and error codes as
+ * snn_propagate; the spike list lives in a file-scope device array of
+ * 1,048,576 entries (4 MiB), so n_pre above 1,048,576 is rejected with
+ * SNN_ERR_ARG.  The first call on a device looks up that array's address
+ * (with the device current), so make it before any stream capture.  Each
+ * call zeroes the list count on `stream` before use.  All calls on one device
+ * share the array: calls that overlap in time on different streams race and
+ * give wrong sums; order them on one stream (or with events). */
+int snn_propagate_static(const int32_t* post, const float* w, int64_t n_pre, int32_t fanout,
+                         const uint8_t* spikes, int32_t* acc, int64_t n_post, int32_t frac_bits,
+                         void* stream);
+
 /* Seeded synthetic UTF-8 byte stream: a fraction p_cjk of characters are
  * CJK code points U+4E00..U+9FFF drawn Zipf(zipf_s) by rank (rank -> code
  * point through a seeded permutation), 3 bytes each; the rest are ASCII

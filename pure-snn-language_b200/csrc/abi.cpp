@@ -234,4 +234,21 @@ int snn_propagate(const int32_t* post, const float* w, int64_t n_pre, int32_t fa
     }
 }
 
+int snn_propagate_static(const int32_t* post, const float* w, int64_t n_pre, int32_t fanout,
+                         const uint8_t* spikes, int32_t* acc, int64_t n_post, int32_t frac_bits,
+                         void* stream) {
+    try {
+        snnb::propagate_static(post, w, n_pre, fanout, spikes, acc, n_post, frac_bits,
+                               (cudaStream_t)stream);
+        g_create_err.clear();
+        return SNN_OK;
+    } catch (const snnb::Error& e) {
+        g_create_err = e.what();
+        return e.code;
+    } catch (const std::exception& e) {
+        g_create_err = e.what();
+        return SNN_ERR_STATE;
+    }
+}
+
 }  // extern "C"

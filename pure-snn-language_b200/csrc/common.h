@@ -89,5 +89,8 @@ Engine* make_engine_stage0(const snn_config& cfg);
 Engine* make_engine_prop(const snn_config& cfg);
 void propagate(const int32_t* post, const float* w, int64_t n_pre, int32_t fanout, const uint8_t* spikes,
                int32_t* acc, int64_t n_post, int32_t frac_bits, cudaStream_t stream);
+void propagate_static(const int32_t* post, const float* w, int64_t n_pre, int32_t fanout,
+                      const uint8_t* spikes, int32_t* acc, int64_t n_post, int32_t frac_bits,
+                      cudaStream_t stream);
 
 }  // namespace snnb

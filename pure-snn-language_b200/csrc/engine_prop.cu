@@ -861,6 +861,22 @@ struct PropScratch {
 };
 PropScratch g_scratch[64];
 
+// Scratch of snn_propagate_static: file-scope device arrays, so that entry
+// point allocates nothing.  The list holds at most STATIC_MAX_PRE spiking
+// neurons; the count is zeroed by every call before the compaction.
+constexpr long long STATIC_MAX_PRE = 1ll << 20;
+static __device__ __align__(256) int32_t g_static_list[STATIC_MAX_PRE];
+static __device__ __align__(256) unsigned g_static_count;
+
+// device addresses of the static scratch, looked up once per device
+struct StaticScratch {
+    std::mutex mu;
+    int32_t* list = nullptr;
+    unsigned* count = nullptr;
+    int sms = 0;
+};
+StaticScratch g_static[64];
+
 }  // namespace
 
 namespace snnb {
@@ -901,5 +917,41 @@ void propagate(const int32_t* post, const float* w, int64_t n_pre, int32_t fanou
     SNN_CUDA(cudaGetLastError());
     SNN_CUDA(cudaEventRecord(sc.done, st));
     sc.recorded = true;
+}
+
+void propagate_static(const int32_t* post, const float* w, int64_t n_pre, int32_t fanout,
+                      const uint8_t* spikes, int32_t* acc, int64_t n_post, int32_t frac_bits,
+                      cudaStream_t st) {
+    SNN_REQUIRE(post && w && spikes && acc, SNN_ERR_ARG, "null device pointer");
+    SNN_REQUIRE(n_pre >= 0 && n_pre <= STATIC_MAX_PRE, SNN_ERR_ARG,
+                "n_pre above the 1,048,576 neurons of the static scratch (use snn_propagate)");
+    SNN_REQUIRE(fanout >= 1, SNN_ERR_ARG, "fanout must be >= 1");
+    SNN_REQUIRE(n_post >= 1 && n_post < (1ll << 31), SNN_ERR_ARG, "n_post must lie in [1, 2^31)");
+    SNN_REQUIRE(frac_bits >= 0 && frac_bits <= 30, SNN_ERR_ARG, "frac_bits must lie in [0, 30]");
+    if (n_pre == 0) return;
+    int dev = 0;
+    SNN_CUDA(cudaGetDevice(&dev));
+    SNN_REQUIRE(dev >= 0 && dev < 64, SNN_ERR_ARG, "device ordinal above 63");
+    StaticScratch& sa = g_static[dev];
+    {
+        std::lock_guard<std::mutex> lk(sa.mu);
+        if (!sa.list) {  // first call on this device (the current one)
+            int32_t* l = nullptr;
+            unsigned* c = nullptr;
+            SNN_CUDA(cudaGetSymbolAddress((void**)&l, g_static_list));
+            SNN_CUDA(cudaGetSymbolAddress((void**)&c, g_static_count));
+            SNN_CUDA(cudaDeviceGetAttribute(&sa.sms, cudaDevAttrMultiProcessorCount, dev));
+            sa.count = c;
+            sa.list = l;
+        }
+    }
+    SNN_CUDA(cudaMemsetAsync(sa.count, 0, 4, st));
+    const long long cb = std::min<long long>((n_pre + P_THREADS - 1) / P_THREADS, (long long)sa.sms * 8);
+    k_compact<<<(unsigned)cb, P_THREADS, 0, st>>>(spikes, n_pre, sa.list, sa.count);
+    const float scale = pm_bits2f((uint32_t)(127 + frac_bits) << 23);
+    const bool vec = (fanout % 4) == 0 && ((uintptr_t)post % 16) == 0 && ((uintptr_t)w % 16) == 0;
+    if (vec) k_push_fixed<true><<<sa.sms * 8, P_THREADS, 0, st>>>(post, w, fanout, sa.list, sa.count, acc, (int)n_post, scale);
+    else k_push_fixed<false><<<sa.sms * 8, P_THREADS, 0, st>>>(post, w, fanout, sa.list, sa.count, acc, (int)n_post, scale);
+    SNN_CUDA(cudaGetLastError());
 }
 }  // namespace snnb

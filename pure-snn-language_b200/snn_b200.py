@@ -97,7 +97,7 @@ EXPORTS = ["snn_config_init", "snn_topology_init", "snn_create", "snn_destroy",
            "snn_last_error", "snn_version", "snn_build_columns", "snn_set_corpus", "snn_step",
            "snn_run", "snn_synchronize", "snn_get_spikes", "snn_get_state", "snn_get_counters",
            "snn_set_dopamine", "snn_set_e0", "snn_save", "snn_load", "snn_stream_generate",
-           "snn_set_profiling", "snn_get_profile", "snn_propagate"]
+           "snn_set_profiling", "snn_get_profile", "snn_propagate", "snn_propagate_static"]
 
 _lib = None
 
@@ -134,22 +134,24 @@ def lib():
         L.snn_set_profiling.argtypes = [vp, C.c_int32]
         L.snn_get_profile.argtypes = [vp, C.POINTER(Profile)]
         L.snn_propagate.argtypes = [vp, vp, C.c_int64, C.c_int32, vp, vp, C.c_int64, C.c_int32, vp]
+        L.snn_propagate_static.argtypes = L.snn_propagate.argtypes
         _lib = L
     return _lib
 
 
-def propagate(post, w, fanout, spikes, acc, frac_bits=24, stream=None):
+def propagate(post, w, fanout, spikes, acc, frac_bits=24, stream=None, static=False):
     """snn_propagate on torch CUDA tensors (int32 post[n_pre*fanout],
     float32 w[...], uint8 spikes[n_pre], int32 acc[n_post], accumulated in
-    place) on `stream` (a torch.cuda.Stream, default: the current stream)."""
+    place) on `stream` (a torch.cuda.Stream, default: the current stream).
+    static=True calls snn_propagate_static (no allocation, n_pre <= 2^20)."""
     import torch
     for t_, dt in ((post, torch.int32), (w, torch.float32), (spikes, torch.uint8), (acc, torch.int32)):
         if not (t_.is_cuda and t_.dtype == dt and t_.is_contiguous()):
             raise SnnError(1, "propagate wants contiguous CUDA tensors int32/float32/uint8/int32")
     st = stream if stream is not None else torch.cuda.current_stream(acc.device)
-    rc = lib().snn_propagate(post.data_ptr(), w.data_ptr(), spikes.numel(), fanout,
-                             spikes.data_ptr(), acc.data_ptr(), acc.numel(), frac_bits,
-                             st.cuda_stream)
+    fn = lib().snn_propagate_static if static else lib().snn_propagate
+    rc = fn(post.data_ptr(), w.data_ptr(), spikes.numel(), fanout, spikes.data_ptr(),
+            acc.data_ptr(), acc.numel(), frac_bits, st.cuda_stream)
     if rc:
         raise SnnError(rc, lib().snn_last_error(None).decode())
 
