@@ -72,6 +72,9 @@ class ClockSampler:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            t0 = time.time()  # let the sampler start before the timed region
+            while not self.rows and time.time() - t0 < 5.0 and self.proc.poll() is None:
+                time.sleep(0.02)
         except OSError:
             self.proc = None
         return self
@@ -195,10 +198,13 @@ def prop_main(args):
     warm = max(args.warmup, 3)
     peak, peak_kind = measured_peaks()
     cb = None if args.no_cpu_baseline else prop_cpu_baseline(0.01)
-    for mode, mname in PROP_MODES:
-        for rate in PROP_RATES:
+    rates = [float(x) for x in args.prop_rates.split(",")] if args.prop_rates else PROP_RATES
+    modes = [m for m in PROP_MODES if not args.prop_modes or str(m[0]) in args.prop_modes.split(",")]
+    n_neu = args.prop_neurons
+    for mode, mname in modes:
+        for rate in rates:
             net = snn.Network(model=snn.MODEL_PROP, prop_mode=mode, prop_rate=rate)
-            net.build_columns(snn.topology(snn.MODEL_PROP))
+            net.build_columns(snn.topology(snn.MODEL_PROP, l4=n_neu))
             net.run(warm)
             net.synchronize()
             c0 = net.counters()
@@ -213,7 +219,8 @@ def prop_main(args):
             ev = c1["arrivals"] - c0["arrivals"]
             pre = c1["dispatched"] - c0["dispatched"]
             dev_s = prof["step_ms"] / 1000.0
-            push = prof["kernels"]["k4_push"]
+            pname = next(k for k in prof["kernels"] if k.startswith("k4_push"))
+            push = prof["kernels"][pname]
             push_s = push["ms"] / push["launches"] / 1000.0
             pb = prop_push_bytes(ev, pre, mode) / args.steps
             achieved = pb / push_s / 1e9
@@ -227,14 +234,14 @@ def prop_main(args):
             wall = time.perf_counter() - t0
             e2e_ev = net.counters()["arrivals"] - ce0["arrivals"]
             line = {
-                "metric": "synaptic events/sec (SOPS), propagation microbench 1M x 1,000",
+                "metric": f"synaptic events/sec (SOPS), propagation microbench {n_neu:,} x 1,000",
                 "value": ev / dev_s, "unit": UNIT, "n_gpus": 1, "steps": args.steps,
                 "warmup": warm, "ms_per_step": prof["step_ms"] / args.steps,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                 "dtype": "f32 weights, int32 fixed-point sums",
                 "data": "synthetic (seeded forced Poisson pre-spikes)",
-                "config": {"workload": f"propagation microbench, 1,000,000 LIF x fan-out 1,000 "
-                                       f"(1.0B synapses), rate {rate}, {mname}",
+                "config": {"workload": f"propagation microbench, {n_neu:,} LIF x fan-out 1,000 "
+                                       f"({n_neu * 1000 / 1e9:.1f}B synapses), rate {rate}, {mname}",
                            "rate": rate, "mode": mname,
                            "events_per_step": ev / args.steps,
                            "post_spikes_per_step": (c1["total_spikes"] - c0["total_spikes"]) / args.steps,
@@ -245,7 +252,7 @@ def prop_main(args):
                 "gpu_launches": int(sum(v["launches"] for v in prof["kernels"].values())),
                 "kernels_ms_per_step": {k: v["ms"] / max(v["launches"], 1)
                                         for k, v in prof["kernels"].items()},
-                "roofline": {"bound": "hbm", "kernel": "k4_push", "achieved": achieved,
+                "roofline": {"bound": "hbm", "kernel": pname, "achieved": achieved,
                              "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                              "peak_kind": peak_kind, "bytes_per_launch": pb, "traffic": None},
                 "clocks": clk.summary(),
@@ -267,6 +274,9 @@ def main():
     ap.add_argument("--workload", default="stage2e", choices=["stage2e", "prop"],
                     help="stage2e: the 55k/10.7M network (one line); prop: the 1M x 1,000 "
                          "propagation microbench (one line per mode and rate, 1 GPU)")
+    ap.add_argument("--prop-neurons", type=int, default=1_000_000)
+    ap.add_argument("--prop-rates", default="", help="comma list, default 0.001,0.01,0.03,0.1")
+    ap.add_argument("--prop-modes", default="", help="comma list of 0 (STDP off), 1 (STDP on), 2 (STP on)")
     args = ap.parse_args()
     warm = max(args.warmup, 3)
     if args.workload == "prop":

@@ -102,7 +102,9 @@ typedef struct snn_config {
     int32_t prop_mode;     /* SNN_MODEL_PROP: SNN_PROP_* flags                 */
     float prop_rate;       /* SNN_MODEL_PROP: forced spike probability per step */
     float prop_w_max;      /* SNN_MODEL_PROP: weight bound (0 = 0.01 / (rate * fan-out)) */
-    int32_t reserved[7];
+    int32_t prop_push;     /* SNN_MODEL_PROP push kernel: 0 auto, 1 one L2 atomic per
+                              synapse, 2 bucketed shared-memory accumulation (same sums) */
+    int32_t reserved[6];
 } snn_config;
 
 /* Network construction by columns and layers.

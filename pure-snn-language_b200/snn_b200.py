@@ -56,7 +56,7 @@ class Config(C.Structure):
     _fields_ = [("model", C.c_int32), ("preset", C.c_int32), ("device", C.c_int32),
                 ("e0", C.c_int32), ("phase_offset", C.c_int32), ("raster_steps", C.c_int32),
                 ("prop_mode", C.c_int32), ("prop_rate", C.c_float), ("prop_w_max", C.c_float),
-                ("reserved", C.c_int32 * 7)]
+                ("prop_push", C.c_int32), ("reserved", C.c_int32 * 6)]
 
 
 class TopologySpec(C.Structure):
@@ -189,7 +189,8 @@ class Network:
     """One network on one GPU (one snn_ctx)."""
 
     def __init__(self, model=MODEL_STAGE2E, preset=PRESET_REF, device=0, e0=False,
-                 phase_offset=0, raster_steps=1024, prop_mode=0, prop_rate=0.01, prop_w_max=0.0):
+                 phase_offset=0, raster_steps=1024, prop_mode=0, prop_rate=0.01, prop_w_max=0.0,
+                 prop_push=0):
         L = lib()
         self.L = L
         cfg = Config()
@@ -197,6 +198,7 @@ class Network:
         cfg.device, cfg.e0, cfg.phase_offset, cfg.raster_steps = device, int(e0), phase_offset, raster_steps
         if model == MODEL_PROP:
             cfg.prop_mode, cfg.prop_rate, cfg.prop_w_max = prop_mode, prop_rate, prop_w_max
+            cfg.prop_push = prop_push
         h = C.c_void_p()
         rc = L.snn_create(C.byref(cfg), C.byref(h))
         if rc:

@@ -15,10 +15,10 @@ def bits(a):
 
 
 def run_pair(n, fanout, rate, mode, steps, chunk=None, seed=42, learn=True, dopamine=None,
-             oracle_mode=None):
+             oracle_mode=None, push=0):
     orc = po.Oracle4(po.prop_params(n=n, fanout=fanout, seed=seed, rate=rate,
                                     mode=mode if oracle_mode is None else oracle_mode))
-    net = snn.Network(model=snn.MODEL_PROP, prop_mode=mode, prop_rate=rate)
+    net = snn.Network(model=snn.MODEL_PROP, prop_mode=mode, prop_rate=rate, prop_push=push)
     net.build_columns(snn.topology(snn.MODEL_PROP, l4=n, deg_intra=fanout, seed=seed))
     assert (net.N, net.S) == (n, n * fanout)
     chunk = chunk or steps
@@ -55,18 +55,22 @@ def run_pair(n, fanout, rate, mode, steps, chunk=None, seed=42, learn=True, dopa
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("push", [1, 2])
 @pytest.mark.parametrize("mode", [0, 1, 2, 3])
 @pytest.mark.parametrize("rate", [0.001, 0.01, 0.1])
-def test_microbench_small(mode, rate):
-    """20,000 neurons x 1,000 out-edges, 300 steps across graph chunks."""
-    oc = run_pair(20000, 1000, rate, mode, 300, chunk=120)
+def test_microbench_small(mode, rate, push):
+    """40,000 neurons (3 post buckets) x 1,000 out-edges, 300 steps across
+    graph chunks, with the L2-atomic push (1) and the bucketed push (2)."""
+    oc = run_pair(40000, 1000, rate, mode, 300, chunk=120, push=push)
     assert oc["total_spikes"] > 0 or mode & snn.PROP_STP
 
 
 @pytest.mark.gpu
 def test_microbench_ragged_fanout():
-    """Fan-out 99 (not a multiple of 4: the scalar push) with STDP + STP."""
-    run_pair(7001, 99, 0.02, 3, 200, chunk=75)
+    """Fan-out 99 (not a multiple of 4: the scalar push) with STDP + STP,
+    and the same through the bucketed push."""
+    run_pair(7001, 99, 0.02, 3, 200, chunk=75, push=1)
+    run_pair(7001, 99, 0.02, 3, 200, chunk=75, push=2)
 
 
 @pytest.mark.gpu
@@ -80,8 +84,8 @@ def test_microbench_learn_off_and_dopamine():
 @pytest.mark.gpu
 def test_microbench_full_size():
     """1,000,000 neurons x 1,000 targets (1.0 B synapses) with STDP at the
-    1 % rate: the benchmark network itself, 40 steps bit-exact (LIF spikes,
-    and so LTP, start after about 25 steps)."""
+    1 % rate (bucketed push): the benchmark network itself, 40 steps bit-exact
+    (LIF spikes, and so LTP, start after about 25 steps)."""
     oc = run_pair(1_000_000, 1000, 0.01, 1, 40, chunk=20)
     assert oc["total_spikes"] > 0 and oc["ltp_visits"] > 0
 
