@@ -107,6 +107,17 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def profile_traffic(name):
+    """DRAM bytes per launch (read + write) recorded from an ncu capture in
+    profiles/<name> as `traffic_bytes_per_launch = N`, or None."""
+    import re
+    p = os.path.join(ROOT, "profiles", name)
+    if not os.path.exists(p):
+        return None
+    m = re.search(r"traffic_bytes_per_launch\s*=\s*([0-9.eE+]+)", open(p).read())
+    return float(m.group(1)) if m else None
+
+
 def synapse_pass_bytes(S, S_exc, d_arr, d_disp, d_ltp, steps, first_step):
     """Algorithmic HBM bytes of the synapse pass over `steps` steps (see
     DESIGN.md, 'Byte model'): group id 4*S + Ca read/write 8*S_exc every
@@ -361,11 +372,7 @@ def main():
     k4_ms = k4["ms"] / k4["launches"]
     peak, peak_kind = measured_peaks()
     achieved = k4_bytes / (k4_ms / 1000.0) / 1e9
-    traffic = None
-    tp = os.path.join(ROOT, "profiles", "traffic_k_synapses.json")
-    if os.path.exists(tp):
-        with open(tp) as f:
-            traffic = json.load(f).get("dram_bytes_per_launch")
+    traffic = profile_traffic("k_synapses_stage2e_55k.md")
 
     # end to end through the C ABI, host buffers
     e2e_steps = args.e2e_steps
