@@ -241,6 +241,28 @@ int snn_get_profile(snn_ctx* ctx, snn_profile* out);
 int snn_save(snn_ctx* ctx, const char* path, int32_t fmt);
 int snn_load(snn_ctx* ctx, const char* path, int32_t fmt);
 
+/* Column sharding of the Stage 2e network over `world` GPUs, one process (and
+ * one snn_ctx) per GPU; call before snn_build_columns.  Rank r owns the
+ * columns [ncol r / world, ncol (r+1) / world) and the prefrontal groups
+ * split the same way, keeps only the synapses onto its neurons, and mirrors
+ * the groups of remote pres; every step all-gathers the ranks' spike
+ * bitmasks, spike counts and TD sub-population counts over NCCL, so the
+ * dynamics stay bit-identical to one GPU.  Rasters, neuron state and
+ * per-synapse state are the rank's own; total_spikes / last_spikes in
+ * snn_get_counters are global, the event counters local.  uid is the
+ * 128-byte ncclUniqueId from snn_nccl_unique_id on one rank, shared with
+ * the others by the caller (no counterpart in the reference, which runs on
+ * one GPU; replaces its single-device MemoryAllocator,
+ * src/stage2e/memory_allocator.cuh:306-339). */
+int snn_nccl_unique_id(uint8_t* out, int64_t n);
+int snn_set_shard(snn_ctx* ctx, int32_t rank, int32_t world, const uint8_t* uid, int64_t n);
+/* Host-only partition plan (no GPU): out[0..9] = local neurons, a0, a1, pf0,
+ * pf1 (the two global neuron ranges), local synapses, groups of local pres,
+ * mirror groups, mirror pres, and the number of local synapses whose remote
+ * pre has an effective delay below 5 steps. */
+int snn_shard_plan(const snn_topology_spec* spec, int32_t rank, int32_t world, int64_t* out,
+                   int32_t n_out);
+
 /* Push propagation of one step's spikes through a fixed-fan-out CSR held in
  * device memory (replaces synaptic_transmission_kernel,
  * src/cuda/synapse_kernel.cu:28-47, whose float atomicAdd order is not

@@ -3,7 +3,9 @@
 #include <cstdio>
 #include <memory>
 #include <string>
+#include <nccl.h>
 #include "common.h"
+#include "net2e.h"
 
 struct snn_ctx {
     snn_config cfg;
@@ -216,6 +218,60 @@ int snn_load(snn_ctx* ctx, const char* path, int32_t fmt) {
         SNN_REQUIRE(path, SNN_ERR_ARG, "null path");
         ctx->eng->load(path, fmt);
     });
+}
+
+int snn_nccl_unique_id(uint8_t* out, int64_t n) {
+    if (!out || n < (int64_t)sizeof(ncclUniqueId)) return SNN_ERR_ARG;
+    ncclUniqueId id;
+    const ncclResult_t r = ncclGetUniqueId(&id);
+    if (r != ncclSuccess) {
+        g_create_err = std::string("ncclGetUniqueId: ") + ncclGetErrorString(r);
+        return SNN_ERR_CUDA;
+    }
+    memcpy(out, &id, sizeof(id));
+    return SNN_OK;
+}
+
+int snn_set_shard(snn_ctx* ctx, int32_t rank, int32_t world, const uint8_t* uid, int64_t n) {
+    return guard(ctx, [&] {
+        SNN_REQUIRE(world == 1 || (uid && n >= (int64_t)sizeof(ncclUniqueId)), SNN_ERR_ARG,
+                    "a 128-byte NCCL unique id is needed for world > 1");
+        ctx->eng->set_shard(rank, world, uid);
+    });
+}
+
+int snn_shard_plan(const snn_topology_spec* spec, int32_t rank, int32_t world, int64_t* out,
+                   int32_t n_out) {
+    if (!spec || !out || n_out < 10) return SNN_ERR_ARG;
+    try {
+        const snn2e::Shard sh = snn2e::make_shard(*spec, rank, world);
+        snn2e::HostNet net;
+        snn2e::generate_reference(*spec, net, &sh);
+        snn2e::Layout lay;
+        snn2e::build_layout(net, lay);
+        int64_t g_local = 0, g_mirror = 0, m = 0, remote_syn = 0, remote_short = 0;
+        for (int gi = 0; gi < net.N; ++gi) {
+            const int64_t ng = lay.gbeg[gi + 1] - lay.gbeg[gi];
+            if (sh.owns(gi)) g_local += ng;
+            else if (ng > 0) { g_mirror += ng; ++m; }
+            if (sh.owns(gi)) continue;
+            for (int32_t sid = net.row_ptr[gi]; sid < net.row_ptr[gi + 1]; ++sid) {
+                ++remote_syn;
+                if (snn2e::eff_delay(net.delay[sid]) < 5) ++remote_short;
+            }
+        }
+        const int64_t vals[10] = {sh.n_local(), sh.a0, sh.a1, sh.pf0, sh.pf1, net.S,
+                                  g_local, g_mirror, m, remote_short};
+        (void)remote_syn;
+        for (int q = 0; q < 10; ++q) out[q] = vals[q];
+        return SNN_OK;
+    } catch (const snnb::Error& e) {
+        g_create_err = e.what();
+        return e.code;
+    } catch (const std::exception& e) {
+        g_create_err = e.what();
+        return SNN_ERR_STATE;
+    }
 }
 
 int snn_propagate(const int32_t* post, const float* w, int64_t n_pre, int32_t fanout,

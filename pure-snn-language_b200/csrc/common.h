@@ -76,6 +76,10 @@ struct Engine {
     virtual void get_spikes(uint32_t* words, int64_t n_words) = 0;
     virtual void set_dopamine(float) { throw Error(SNN_ERR_UNSUPPORTED, "no dopamine control in this model"); }
     virtual void set_e0(int32_t) { throw Error(SNN_ERR_UNSUPPORTED, "no E0 ablation in this model"); }
+    // column sharding over `world` ranks (one per GPU); uid = ncclUniqueId
+    virtual void set_shard(int32_t, int32_t, const void*) {
+        throw Error(SNN_ERR_UNSUPPORTED, "this model does not shard");
+    }
     virtual void save(const char* path, int32_t fmt) = 0;
     virtual void load(const char* path, int32_t fmt) = 0;
     virtual int64_t steps_done() const = 0;

@@ -37,6 +37,7 @@
 #include <cmath>
 #include <cstdio>
 #include <memory>
+#include <nccl.h>
 #include "common.h"
 #include "net2e.h"
 #include "snn_pmath.h"
@@ -129,6 +130,20 @@ struct Dev {
     int N, N_assoc, NPC, ncol, l4, per_sub;
     int tile_cap;           // staged elements per stream per buffer (>= any aligned in-list)
     int queue_cap;          // per-warp event queue entries (>= max in-degree)
+    // column sharding: local neuron j is global a0 + j for j < n_a, else
+    // pf0 + (j - n_a).  With sharded != 0 the step's spike words, spike count
+    // and TD sub-population counts go to `send`, every rank's payload arrives
+    // in `recv` (an all-gather between k_neurons and k_mirror), and the
+    // groups of remote pres ("mirror" groups, after the local ones) are
+    // updated by k_mirror from the gathered bits.
+    int n_a, a0, pf0, sharded, world;
+    unsigned* send;
+    const unsigned* recv;
+    int pw, words_max;      // payload words per rank; count word index
+    int M;                  // mirror pres
+    const int* mbeg;        // M + 1 group ranges
+    const unsigned* mbit;   // bit of each mirror pre in recv
+    unsigned* mhist;        // 32-step spike history of each mirror pre
 };
 
 __device__ __forceinline__ int phase_of(long long step) {
@@ -207,6 +222,8 @@ __global__ void __launch_bounds__(64) k_control(Dev d, Consts k) {
         d.l6_sp[(t & 1) * d.ncol + q] = 0;
     }
     for (int q = tid; q < TD_DIM; q += blockDim.x) d.sub_sp[(t & 1) * TD_DIM + q] = 0;
+    if (d.sharded)
+        for (int q = tid; q < 1 + TD_DIM; q += blockDim.x) d.send[d.words_max + q] = 0u;
     for (int col = tid; col < d.ncol; col += blockDim.x) {
         float4 g = d.gates[col];
         const float cur = prev_ok ? pm_i2f(d.col_sp[((t - 1) & 1) * d.ncol + col]) : 0.0f;
@@ -305,6 +322,44 @@ __device__ void step_epilogue(const Dev& d, const Consts& k) {
     if (arr > 750000ull) c->dropped_ref += arr - 750000ull;
 }
 
+// STP / NMDA / pre-trace update of group g at step t from its pre's spike
+// history h (bit 0 = spike at t, bit d = spike at t - d) and its per-step
+// view for the synapse pass
+__device__ __forceinline__ void update_group(const Dev& d, const Consts& k, int g, unsigned meta, float4 st,
+                                             unsigned h, unsigned long long& arr_cnt,
+                                             unsigned long long& disp_cnt) {
+    const int dd = meta & GV_D_MASK;
+    const bool ff = meta & GV_FF, exc = meta & GV_EXC;
+    const bool arr = (h >> dd) & 1u;
+    const bool nxt = (h >> (dd - 1)) & 1u;
+    const bool disp = h & 1u;
+    if (arr && exc) st.z = pm_fma(pm_mul(k.g_nmda, st.x), st.y, st.z);
+    st.z = pm_mul(st.z, k.dec_nmda);
+    if (ff) st.x = pm_fma(pm_sub(1.0f, st.x), k.rec_ff_step, st.x);
+    st.w = pm_mul(st.w, k.dec_xpre);
+    const float x_ltp = st.w;
+    if (arr) {
+        st.w = pm_add(st.w, k.a_plus);
+        const int cl = ff ? 0 : (exc ? 1 : 2);
+        const float U = k.U[cl];
+        st.x = pm_fma(pm_sub(1.0f, st.x), k.rec[cl], st.x);
+        st.y = pm_fma(pm_sub(st.y, U), k.fac[cl], U);
+        const float un = pm_fma(U, pm_sub(1.0f, st.y), st.y);
+        const float rn = pm_mul(st.x, pm_sub(1.0f, un));
+        st.y = un > 1.0f ? 1.0f : un;
+        st.x = rn < 0.0f ? 0.0f : rn;
+        arr_cnt += gw_size(meta);
+    }
+    if (disp) disp_cnt += gw_size(meta);
+    d.gstate[g] = st;
+    const bool ring = nxt && dd >= 2;
+    const unsigned fl = (meta & (GV_D_MASK | GV_FF | GV_EXC)) | (arr ? GV_ARR : 0u) |
+                        (nxt ? GV_NEXT : 0u) | (disp ? GV_DISP : 0u) |
+                        ((arr || disp || ring) ? GV_EV : 0u);
+    d.gview[g] = make_float2(st.z, __uint_as_float(fl));
+    d.gcold[g] = make_float2(x_ltp, st.x);
+}
+
 // ---------------------------------------------------------------------------
 // k_neurons: one thread per neuron, then the CTA's outgoing synapse groups.
 //   input .......... input_encoding.cu:117-164 (hashes recomputed per L4 neuron,
@@ -321,6 +376,7 @@ __global__ void __launch_bounds__(NEU_BLOCK) k_neurons(Dev d, Consts k) {
     __shared__ unsigned s_hist[NEU_BLOCK];
     const Ctrl* c = d.ctrl;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    const int gi = i < d.n_a ? d.a0 + i : d.pf0 + (i - d.n_a);  // global neuron id
     const long long t = c->t;
     const bool valid = i < d.N;
     unsigned spike = 0;
@@ -331,7 +387,7 @@ __global__ void __launch_bounds__(NEU_BLOCK) k_neurons(Dev d, Consts k) {
         const int col = (region != PF) ? (int)(info >> 8) : -1;
         float input = d.input[i];
         if (c->inject && region == L4) {
-            const int off = i - col * d.NPC;
+            const int off = gi - col * d.NPC;
             const int b = c->byte;
             const int ps = col * k.pref_range;
             const bool in_r = b >= ps && b < ps + k.pref_range;
@@ -355,7 +411,7 @@ __global__ void __launch_bounds__(NEU_BLOCK) k_neurons(Dev d, Consts k) {
                 const int kk = c->kwta_k;
                 int width = kk * 8;
                 width = width < 1 ? 1 : (width > d.NPC ? d.NPC : width);
-                const int rank = (i + col * 37) % d.NPC;
+                const int rank = (gi + col * 37) % d.NPC;
                 if (sp > 0 && sp > kk && rank >= width) {
                     float ex = pm_mul(0.35f, pm_div(pm_i2f(sp - kk), pm_i2f(kk + 1)));
                     if (ex > 2.0f) ex = 2.0f;
@@ -421,8 +477,14 @@ __global__ void __launch_bounds__(NEU_BLOCK) k_neurons(Dev d, Consts k) {
         hist = (d.hist[i] << 1) | spike;
         d.hist[i] = hist;
         if (spike) {
-            atomicAdd(&d.ctrl->step_spikes[t & 1], 1);
-            if (i / d.per_sub < TD_DIM) atomicAdd(&d.sub_sp[(t & 1) * TD_DIM + i / d.per_sub], 1);
+            const int sub = gi / d.per_sub;
+            if (d.sharded) {  // global counts are summed over the ranks by k_mirror
+                atomicAdd(&d.send[d.words_max], 1u);
+                if (sub < TD_DIM) atomicAdd(&d.send[d.words_max + 1 + sub], 1u);
+            } else {
+                atomicAdd(&d.ctrl->step_spikes[t & 1], 1);
+                if (sub < TD_DIM) atomicAdd(&d.sub_sp[(t & 1) * TD_DIM + sub], 1);
+            }
             if (col >= 0) {
                 atomicAdd(&d.col_sp[(t & 1) * d.ncol + col], 1);
                 if (region == L6) atomicAdd(&d.l6_sp[(t & 1) * d.ncol + col], 1);
@@ -439,6 +501,7 @@ __global__ void __launch_bounds__(NEU_BLOCK) k_neurons(Dev d, Consts k) {
     if ((threadIdx.x & 31) == 0 && (i >> 5) < d.words) {
         const long long row = (t - c->raster_base) % d.raster_cap;
         d.raster[row * d.words + (i >> 5)] = word;
+        if (d.sharded) d.send[i >> 5] = word;
     }
     __syncthreads();
     // outgoing synapse groups of this CTA's neurons, one thread per group
@@ -447,37 +510,7 @@ __global__ void __launch_bounds__(NEU_BLOCK) k_neurons(Dev d, Consts k) {
     const int g0 = d.gbeg[i0], g1 = d.gbeg[i1];
     unsigned long long arr_cnt = 0, disp_cnt = 0;
     auto group_update = [&](int g, unsigned meta, float4 st) {
-        const unsigned h = s_hist[gw_lpre(meta)];
-        const int dd = meta & GV_D_MASK;
-        const bool ff = meta & GV_FF, exc = meta & GV_EXC;
-        const bool arr = (h >> dd) & 1u;
-        const bool nxt = (h >> (dd - 1)) & 1u;
-        const bool disp = h & 1u;
-        if (arr && exc) st.z = pm_fma(pm_mul(k.g_nmda, st.x), st.y, st.z);
-        st.z = pm_mul(st.z, k.dec_nmda);
-        if (ff) st.x = pm_fma(pm_sub(1.0f, st.x), k.rec_ff_step, st.x);
-        st.w = pm_mul(st.w, k.dec_xpre);
-        const float x_ltp = st.w;
-        if (arr) {
-            st.w = pm_add(st.w, k.a_plus);
-            const int cl = ff ? 0 : (exc ? 1 : 2);
-            const float U = k.U[cl];
-            st.x = pm_fma(pm_sub(1.0f, st.x), k.rec[cl], st.x);
-            st.y = pm_fma(pm_sub(st.y, U), k.fac[cl], U);
-            const float un = pm_fma(U, pm_sub(1.0f, st.y), st.y);
-            const float rn = pm_mul(st.x, pm_sub(1.0f, un));
-            st.y = un > 1.0f ? 1.0f : un;
-            st.x = rn < 0.0f ? 0.0f : rn;
-            arr_cnt += gw_size(meta);
-        }
-        if (disp) disp_cnt += gw_size(meta);
-        d.gstate[g] = st;
-        const bool ring = nxt && dd >= 2;
-        const unsigned fl = (meta & (GV_D_MASK | GV_FF | GV_EXC)) | (arr ? GV_ARR : 0u) |
-                            (nxt ? GV_NEXT : 0u) | (disp ? GV_DISP : 0u) |
-                            ((arr || disp || ring) ? GV_EV : 0u);
-        d.gview[g] = make_float2(st.z, __uint_as_float(fl));
-        d.gcold[g] = make_float2(x_ltp, st.x);
+        update_group(d, k, g, meta, st, s_hist[gw_lpre(meta)], arr_cnt, disp_cnt);
     };
     // two groups per iteration keep independent loads in flight
     const int stride = 2 * blockDim.x;
@@ -489,6 +522,50 @@ __global__ void __launch_bounds__(NEU_BLOCK) k_neurons(Dev d, Consts k) {
         const float4 s1 = g2 < g1 ? d.gstate[g2] : make_float4(0, 0, 0, 0);
         group_update(g, m0, s0);
         if (g2 < g1) group_update(g2, m1, s1);
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+        arr_cnt += __shfl_xor_sync(0xffffffffu, arr_cnt, o);
+        disp_cnt += __shfl_xor_sync(0xffffffffu, disp_cnt, o);
+    }
+    if ((threadIdx.x & 31) == 0) {
+        if (arr_cnt) {
+            atomicAdd(&d.ctrl->arrivals, arr_cnt);
+            atomicAdd(&d.ctrl->step_arrivals[t & 1], arr_cnt);
+        }
+        if (disp_cnt) atomicAdd(&d.ctrl->dispatched, disp_cnt);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// k_mirror (sharded runs): after the all-gather of step t's payloads, the
+// global spike count and TD sub-population counts of step t (block 0), then
+// one thread per mirror pre: its history gains the gathered bit of step t and
+// its groups (synapses onto this rank's neurons) get the same update the
+// owning rank's k_neurons gives a local pre's groups.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(NEU_BLOCK) k_mirror(Dev d, Consts k) {
+    const long long t = d.ctrl->t;
+    if (blockIdx.x == 0) {
+        if (threadIdx.x == 0) {
+            long long cnt = 0;
+            for (int r = 0; r < d.world; ++r) cnt += d.recv[(size_t)r * d.pw + d.words_max];
+            d.ctrl->step_spikes[t & 1] = (int)cnt;
+        }
+        for (int q = threadIdx.x; q < TD_DIM; q += blockDim.x) {
+            int sc = 0;
+            for (int r = 0; r < d.world; ++r) sc += (int)d.recv[(size_t)r * d.pw + d.words_max + 1 + q];
+            d.sub_sp[(t & 1) * TD_DIM + q] = sc;
+        }
+    }
+    const int m = blockIdx.x * blockDim.x + threadIdx.x;
+    unsigned long long arr_cnt = 0, disp_cnt = 0;
+    if (m < d.M) {
+        const unsigned b = d.mbit[m];
+        const unsigned h = (d.mhist[m] << 1) | ((d.recv[b >> 5] >> (b & 31)) & 1u);
+        d.mhist[m] = h;
+        const int ge = d.mbeg[m + 1];
+        for (int g = d.mbeg[m]; g < ge; ++g) update_group(d, k, g, d.gmeta[g], d.gstate[g], h, arr_cnt, disp_cnt);
     }
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) {
@@ -891,6 +968,15 @@ struct Engine2e : snnb::Engine {
     snnb::DevBuf<int> counts_tmp;
     int tile_cap = 0, syn_grid = 1, queue_cap = 0;
     size_t syn_smem = 0;
+    // column sharding (world > 1): NCCL communicator, this rank's ranges,
+    // payload buffers and the mirror groups of remote pres
+    int rank = 0, world = 1;
+    ncclComm_t comm = nullptr;
+    Shard sh;
+    std::vector<int64_t> new_of_old;  // layout group id -> device group id
+    snnb::DevBuf<unsigned> send, recv, mbit, mhist;
+    snnb::DevBuf<int> mbeg;
+    int64_t G_local = 0;              // groups of local pres (the rest mirror remote pres)
 
     explicit Engine2e(const snn_config& c) : cfg(c) {
         if (cfg.raster_steps > 0) raster_cap = cfg.raster_steps;
@@ -900,10 +986,12 @@ struct Engine2e : snnb::Engine {
     }
     ~Engine2e() override {
         for (auto e : pev) cudaEventDestroy(e);
+        // graphs holding NCCL calls go before the communicator
         if (graph_exec) cudaGraphExecDestroy(graph_exec);
         if (graph) cudaGraphDestroy(graph);
+        if (stream) cudaStreamSynchronize(stream);
+        if (comm) ncclCommDestroy(comm);
         if (stream) {
-            cudaStreamSynchronize(stream);
             cudaStreamDestroy(stream);
         }
     }
@@ -950,17 +1038,38 @@ struct Engine2e : snnb::Engine {
         k.pop_gain = 80.0f; k.gain_in = 2.0f; k.gain_out = 0.03f; k.pop_k = 100; k.inject_interval = 3;
     }
 
+    void set_shard(int32_t r, int32_t w, const void* uid) override {
+        SNN_REQUIRE(!built, SNN_ERR_STATE, "shard before building the network");
+        SNN_REQUIRE(w >= 1 && r >= 0 && r < w, SNN_ERR_ARG, "bad rank / world size");
+        rank = r;
+        world = w;
+        if (w > 1) {
+            SNN_REQUIRE(uid, SNN_ERR_ARG, "null NCCL unique id");
+            ncclUniqueId id;
+            memcpy(&id, uid, sizeof(id));
+            SNN_CUDA(cudaSetDevice(cfg.device));
+            ncclResult_t nr = ncclCommInitRank(&comm, w, id, r);
+            SNN_REQUIRE(nr == ncclSuccess, SNN_ERR_CUDA,
+                        std::string("ncclCommInitRank: ") + ncclGetErrorString(nr));
+        }
+    }
+
     void build(const snn_topology_spec& spec) override {
         SNN_REQUIRE(!built, SNN_ERR_STATE, "network already built");
         SNN_REQUIRE(spec.rule == 0, SNN_ERR_UNSUPPORTED, "stage2e supports the reference rule only");
-        generate_reference(spec, net);
+        sh = make_shard(spec, rank, world);
+        generate_reference(spec, net, &sh);
         build_layout(net, lay);
         K.pref_range = 256 / net.ncol;
-        const int N = net.N;
+        const int NG = net.N;          // all neurons
+        const int N = sh.n_local();    // this rank's neurons
         const int64_t S = net.S, G = lay.G;
         D.N = N; D.N_assoc = net.N_assoc; D.NPC = net.NPC; D.ncol = net.ncol; D.l4 = net.l4;
-        D.per_sub = N / TD_DIM;
+        D.per_sub = NG / TD_DIM;
         SNN_REQUIRE(D.per_sub > 0, SNN_ERR_ARG, "network too small for the 200-dim value function");
+        D.n_a = sh.a1 - sh.a0; D.a0 = sh.a0; D.pf0 = sh.pf0;
+        D.sharded = world > 1 ? 1 : 0;
+        D.world = world;
         D.words = (N + 31) / 32;
         D.raster_cap = raster_cap;
         // neurons
@@ -972,39 +1081,100 @@ struct Engine2e : snnb::Engine {
         std::vector<int> h_last(N, -1000);
         last.upload(h_last.data(), N, stream);
         std::vector<unsigned> h_info(N);
+        std::vector<int> h_in(N + 1);
         for (int i = 0; i < N; ++i) {
-            unsigned colf = net.column[i] < 0 ? 0xffffffu : (unsigned)net.column[i];
-            h_info[i] = (unsigned)net.type[i] | ((unsigned)net.region[i] << 1) |
-                        ((unsigned)net.subtype[i] << 4) | (colf << 8);
+            const int gi = sh.global_of(i);
+            unsigned colf = net.column[gi] < 0 ? 0xffffffu : (unsigned)net.column[gi];
+            h_info[i] = (unsigned)net.type[gi] | ((unsigned)net.region[gi] << 1) |
+                        ((unsigned)net.subtype[gi] << 4) | (colf << 8);
+            h_in[i] = lay.in_ptr[gi];  // only local neurons have incoming synapses here
         }
+        h_in[N] = lay.in_ptr[NG];
         info.upload(h_info.data(), N, stream);
-        gbeg.upload(lay.gbeg.data(), N + 1, stream);
-        in_ptr.upload(lay.in_ptr.data(), N + 1, stream);
-        // groups
+        in_ptr.upload(h_in.data(), N + 1, stream);
+        // groups: those of local pres in local order, then the mirror groups
+        // of remote pres (ascending global id)
+        new_of_old.assign(G, -1);
+        std::vector<int64_t> order;
+        order.reserve(G);
+        std::vector<int> h_gbeg(N + 1), h_mbeg;
+        std::vector<unsigned> h_mbit;
+        for (int i = 0; i < N; ++i) {
+            const int gi = sh.global_of(i);
+            h_gbeg[i] = (int)order.size();
+            for (int g = lay.gbeg[gi]; g < lay.gbeg[gi + 1]; ++g) order.push_back(g);
+        }
+        h_gbeg[N] = (int)order.size();
+        G_local = (int64_t)order.size();
+        std::vector<Shard> all(world);
+        for (int r = 0; r < world; ++r) all[r] = make_shard(spec, r, world);
+        int words_max = 0;
+        for (int r = 0; r < world; ++r) words_max = std::max(words_max, (all[r].n_local() + 31) / 32);
+        const int pw = words_max + 1 + TD_DIM;
+        for (int gi = 0; gi < NG; ++gi) {
+            if (sh.owns(gi) || lay.gbeg[gi] == lay.gbeg[gi + 1]) continue;
+            int owner = -1;
+            for (int r = 0; r < world && owner < 0; ++r)
+                if (all[r].owns(gi)) owner = r;
+            SNN_REQUIRE(owner >= 0, SNN_ERR_STATE, "neuron without an owning shard");
+            h_mbeg.push_back((int)order.size());
+            h_mbit.push_back((unsigned)((int64_t)owner * pw * 32 + all[owner].local_of(gi)));
+            for (int g = lay.gbeg[gi]; g < lay.gbeg[gi + 1]; ++g) order.push_back(g);
+        }
+        h_mbeg.push_back((int)order.size());
+        SNN_REQUIRE((int64_t)order.size() == G, SNN_ERR_STATE, "group reordering lost groups");
+        SNN_REQUIRE((int64_t)world * pw * 32 < (1ll << 32), SNN_ERR_ARG, "exchange payload too large");
+        for (int64_t x = 0; x < G; ++x) new_of_old[order[x]] = x;
+        D.M = (int)h_mbit.size();
+        D.pw = pw;
+        D.words_max = words_max;
+        gbeg.upload(h_gbeg.data(), N + 1, stream);
         gmeta.alloc(G); gsize.alloc(G); gstate.alloc(G); gview.alloc(G); gcold.alloc(G);
         {
             std::vector<unsigned> packed(G);
-            for (int64_t g = 0; g < G; ++g) {
+            std::vector<int> h_gsize(G), h_gpre(G);
+            std::vector<float4> h_gs(G);
+            for (int64_t x = 0; x < G; ++x) {
+                const int64_t g = order[x];
                 SNN_REQUIRE(lay.gsize[g] < 65536, SNN_ERR_ARG, "synapse group too large");
-                packed[g] = (lay.gmeta[g] & 0x7fu) | ((unsigned)lay.gsize[g] << 8) |
-                            ((unsigned)(lay.gpre[g] % NEU_BLOCK) << 24);
+                const unsigned lpre = x < G_local ? (unsigned)(sh.local_of(lay.gpre[g]) % NEU_BLOCK) : 0u;
+                packed[x] = (lay.gmeta[g] & 0x7fu) | ((unsigned)lay.gsize[g] << 8) | (lpre << 24);
+                h_gsize[x] = lay.gsize[g];
+                h_gpre[x] = lay.gpre[g];
+                h_gs[x] = make_float4(1.0f, lay.gu0[g], 0.0f, 0.0f);
             }
             gmeta.upload(packed.data(), G, stream);
+            gsize.upload(h_gsize.data(), G, stream);
+            gpre.alloc(G);
+            gpre.upload(h_gpre.data(), G, stream);
+            gstate.upload(h_gs.data(), G, stream);
+            SNN_CUDA(cudaStreamSynchronize(stream));
         }
-        gsize.upload(lay.gsize.data(), G, stream);
-        gpre.alloc(G);
-        gpre.upload(lay.gpre.data(), G, stream);
-        std::vector<float4> h_gs(G);
-        for (int64_t g = 0; g < G; ++g) h_gs[g] = make_float4(1.0f, lay.gu0[g], 0.0f, 0.0f);
-        gstate.upload(h_gs.data(), G, stream);
         gview.zero(stream);
         gcold.zero(stream);
+        mbeg.alloc(h_mbeg.size());
+        mbeg.upload(h_mbeg.data(), h_mbeg.size(), stream);
+        mbit.alloc(std::max<size_t>(h_mbit.size(), 1));
+        if (!h_mbit.empty()) mbit.upload(h_mbit.data(), h_mbit.size(), stream);
+        mhist.alloc(std::max<size_t>(h_mbit.size(), 1));
+        mhist.zero(stream);
+        if (world > 1) {
+            send.alloc(pw);
+            send.zero(stream);
+            recv.alloc((size_t)world * pw);
+            recv.zero(stream);
+        }
         // synapses, post-major
         // gid / ca are streamed in 16-byte aligned tiles: pad by 4 elements
         gid.alloc(S + 4); ca.alloc(S + 4); ev.alloc(S); act.alloc(S); e1.alloc(S); e2.alloc(S);
         val.alloc((size_t)S * VAL_SLOTS);
         gid.zero(stream);
+        for (int64_t p = 0; p < S; ++p) {  // layout group ids -> device group ids
+            const uint32_t v = lay.gid_pm[p];
+            lay.gid_pm[p] = (uint32_t)new_of_old[v & 0x3fffffffu] | (v & 0xc0000000u);
+        }
         gid.upload(lay.gid_pm.data(), S, stream);
+        SNN_CUDA(cudaStreamSynchronize(stream));
         {   // plasticity records {alpha, beta, auto, elig}, post-major
             std::vector<float4> h_ev(S);
             for (int64_t p = 0; p < S; ++p) {
@@ -1017,7 +1187,7 @@ struct Engine2e : snnb::Engine {
         // synapse pass: per-warp staging buffers sized by the largest in-degree
         {
             int max_in = 0;
-            for (int j = 0; j < N; ++j) max_in = std::max(max_in, lay.in_ptr[j + 1] - lay.in_ptr[j]);
+            for (int j = 0; j < N; ++j) max_in = std::max(max_in, h_in[j + 1] - h_in[j]);
             SNN_REQUIRE(max_in < 65536, SNN_ERR_ARG, "in-degree above 65535");
             tile_cap = ((max_in + 6) + 3) & ~3;   // aligned range of any neuron's list
             queue_cap = (max_in + 31) & ~31;
@@ -1070,6 +1240,7 @@ struct Engine2e : snnb::Engine {
         D.byte_hist_nov = byte_hist_nov.p; D.byte_histogram = byte_histogram.p;
         D.neuron_byte_counts = neuron_byte_counts.p; D.w_value = w_value.p; D.w_pred = w_pred.p;
         D.baseline = baseline.p; D.corpus = corpus.p; D.raster = raster.p;
+        D.send = send.p; D.recv = recv.p; D.mbeg = mbeg.p; D.mbit = mbit.p; D.mhist = mhist.p;
     }
 
     void set_corpus(const uint8_t* b, int64_t n) override {
@@ -1098,25 +1269,34 @@ struct Engine2e : snnb::Engine {
         graph_steps = 0;
     }
 
-    // one step; with profiling, events ev[0..3] bracket the three kernels
+    // kernels (timing slots) per step: control, neurons, [exchange + mirror
+    // groups when sharded], synapses
+    int nslot() const { return world > 1 ? 4 : 3; }
+
+    // one step; with profiling, events ev[0..nslot] bracket the slots
     // (inside a stream capture the records must be "external" so that they
     // become event-record nodes that time the graph's kernels)
     void launch_step(cudaStream_t st, cudaEvent_t* ev = nullptr, bool capturing = false) {
         const int nb = (D.N + NEU_BLOCK - 1) / NEU_BLOCK;
-        const long long warps = D.N;
         const unsigned fl = capturing ? cudaEventRecordExternal : cudaEventRecordDefault;
-        if (ev) SNN_CUDA(cudaEventRecordWithFlags(ev[0], st, fl));
+        int e = 0;
+        if (ev) SNN_CUDA(cudaEventRecordWithFlags(ev[e++], st, fl));
         k_control<<<1, 64, 0, st>>>(D, K);
-        if (ev) SNN_CUDA(cudaEventRecordWithFlags(ev[1], st, fl));
+        if (ev) SNN_CUDA(cudaEventRecordWithFlags(ev[e++], st, fl));
         k_neurons<<<nb, NEU_BLOCK, 0, st>>>(D, K);
-        if (ev) SNN_CUDA(cudaEventRecordWithFlags(ev[2], st, fl));
-        (void)warps;
+        if (ev) SNN_CUDA(cudaEventRecordWithFlags(ev[e++], st, fl));
+        if (world > 1) {
+            const ncclResult_t nr = ncclAllGather(send.p, recv.p, (size_t)D.pw, ncclUint32, comm, st);
+            SNN_REQUIRE(nr == ncclSuccess, SNN_ERR_CUDA, std::string("ncclAllGather: ") + ncclGetErrorString(nr));
+            k_mirror<<<std::max(1, (D.M + NEU_BLOCK - 1) / NEU_BLOCK), NEU_BLOCK, 0, st>>>(D, K);
+            if (ev) SNN_CUDA(cudaEventRecordWithFlags(ev[e++], st, fl));
+        }
         k_synapses<<<syn_grid, SYN_THREADS, syn_smem, st>>>(D, K);
-        if (ev) SNN_CUDA(cudaEventRecordWithFlags(ev[3], st, fl));
+        if (ev) SNN_CUDA(cudaEventRecordWithFlags(ev[e++], st, fl));
     }
 
     void ensure_events(int n_steps) {
-        size_t need = (size_t)n_steps * 3 + 1;
+        size_t need = (size_t)n_steps * (nslot() + 1);
         while (pev.size() < need) {
             cudaEvent_t e;
             SNN_CUDA(cudaEventCreate(&e));
@@ -1130,16 +1310,17 @@ struct Engine2e : snnb::Engine {
     // eligibility schedule), which move most bytes
     void harvest(int n, long long t0) {
         SNN_CUDA(cudaStreamSynchronize(stream));
+        const int ns = nslot();
         for (int q = 0; q < n; ++q) {
-            for (int kk = 0; kk < 3; ++kk) {
+            for (int kk = 0; kk < ns; ++kk) {
                 float ms = 0.0f;
-                SNN_CUDA(cudaEventElapsedTime(&ms, pev[3 * q + kk], pev[3 * q + kk + 1]));
+                SNN_CUDA(cudaEventElapsedTime(&ms, pev[ns * q + kk], pev[ns * q + kk + 1]));
                 prof.kernel_ms[kk] += ms;
                 prof.launches[kk] += 1;
                 prof.step_ms += ms;
-                if (kk == 2 && (t0 + q) % 10 == 0) {
-                    prof.kernel_ms[3] += ms;
-                    prof.launches[3] += 1;
+                if (kk == ns - 1 && (t0 + q) % 10 == 0) {
+                    prof.kernel_ms[ns] += ms;
+                    prof.launches[ns] += 1;
                 }
             }
         }
@@ -1152,7 +1333,7 @@ struct Engine2e : snnb::Engine {
         drop_graph();
         if (profiling) ensure_events(n);
         SNN_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
-        for (int q = 0; q < n; ++q) launch_step(stream, profiling ? &pev[3 * q] : nullptr, true);
+        for (int q = 0; q < n; ++q) launch_step(stream, profiling ? &pev[(size_t)nslot() * q] : nullptr, true);
         SNN_CUDA(cudaStreamEndCapture(stream, &graph));
         SNN_CUDA(cudaGraphInstantiate(&graph_exec, graph, 0));
         graph_steps = n;
@@ -1164,11 +1345,13 @@ struct Engine2e : snnb::Engine {
         profiling = en != 0;
         drop_graph();
         memset(&prof, 0, sizeof(prof));
-        prof.n_kernels = 4;
-        strcpy(prof.names[0], "k_control");
-        strcpy(prof.names[1], "k_neurons");
-        strcpy(prof.names[2], "k_synapses");
-        strcpy(prof.names[3], "k_synapses@t%10==0");
+        int q = 0;
+        strcpy(prof.names[q++], "k_control");
+        strcpy(prof.names[q++], "k_neurons");
+        if (world > 1) strcpy(prof.names[q++], "allgather+k_mirror");
+        strcpy(prof.names[q++], "k_synapses");
+        strcpy(prof.names[q++], "k_synapses@t%10==0");
+        prof.n_kernels = q;
     }
 
     void get_profile(snn_profile* o) override { *o = prof; }
@@ -1266,7 +1449,7 @@ struct Engine2e : snnb::Engine {
         o->dropped_ref = (int64_t)h.dropped_ref;
         o->ltp_visits = (int64_t)h.ltp_visits;
         o->burst_spikes = (int64_t)h.burst;
-        o->n_neurons = net.N;
+        o->n_neurons = D.N;   // this rank's neurons (all of them unsharded)
         o->n_synapses = net.S;
         o->n_groups = lay.G;
         o->last_spikes = steps > 0 ? h.step_spikes[(steps - 1) & 1] : 0;
@@ -1310,7 +1493,8 @@ struct Engine2e : snnb::Engine {
 
     void get_state(int32_t which, void* buf, int64_t nbytes) override {
         SNN_REQUIRE(built, SNN_ERR_STATE, "build the network first");
-        const int N = net.N;
+        const int N = D.N;    // this rank's neurons
+        const int NG = net.N; // pres of the kept synapses' row pointer
         const int64_t S = net.S;
         auto need = [&](int64_t bytes) {
             SNN_REQUIRE(nbytes >= bytes, SNN_ERR_ARG, "state buffer too small");
@@ -1336,7 +1520,7 @@ struct Engine2e : snnb::Engine {
             need(S * 4);
             auto gs = fetch(gstate, lay.G);
             float* o = (float*)buf;
-            for (int pre = 0; pre < N; ++pre) {
+            for (int pre = 0; pre < NG; ++pre) {
                 for (int32_t sid = net.row_ptr[pre]; sid < net.row_ptr[pre + 1]; ++sid) {
                     int key = eff_delay(net.delay[sid]) * 2 + ((net.flags[sid] & RF_FF) ? 1 : 0);
                     int g = lay.gbeg[pre];
@@ -1345,7 +1529,7 @@ struct Engine2e : snnb::Engine {
                         if ((int)((m & GV_D_MASK) * 2 + ((m & GV_FF) ? 1 : 0)) == key) break;
                         ++g;
                     }
-                    const float4 v = gs[g];
+                    const float4 v = gs[new_of_old[g]];
                     float x = comp == 0 ? v.x : comp == 1 ? v.y : comp == 2 ? v.z : v.w;
                     // inhibitory synapses never gain NMDA conductance
                     o[sid] = x;
@@ -1403,7 +1587,7 @@ struct Engine2e : snnb::Engine {
             case SNN_STATE_POST: need(S * 4); memcpy(buf, net.post.data(), S * 4); break;
             case SNN_STATE_DELAY: need(S); memcpy(buf, net.delay.data(), S); break;
             case SNN_STATE_FLAGS: need(S); memcpy(buf, net.flags.data(), S); break;
-            case SNN_STATE_ROW_PTR: need((int64_t)(N + 1) * 4); memcpy(buf, net.row_ptr.data(), (N + 1) * 4); break;
+            case SNN_STATE_ROW_PTR: need((int64_t)(NG + 1) * 4); memcpy(buf, net.row_ptr.data(), (NG + 1) * 4); break;
             case SNN_STATE_GATES: {
                 need((int64_t)net.ncol * 16);
                 gates.download((float4*)buf, net.ncol, stream);

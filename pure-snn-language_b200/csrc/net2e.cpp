@@ -24,7 +24,27 @@ struct XorShift32 {  // src/stage2e/network_init.cu:167-179
 };
 }  // namespace
 
-void generate_reference(const snn_topology_spec& sp, HostNet& n) {
+Shard make_shard(const snn_topology_spec& sp, int rank, int world) {
+    SNN_REQUIRE(world >= 1 && rank >= 0 && rank < world, SNN_ERR_ARG, "bad shard rank / world");
+    SNN_REQUIRE(sp.n_columns >= world && sp.pf_groups >= world, SNN_ERR_ARG,
+                "fewer columns or prefrontal groups than shards");
+    const int NPC = sp.l4 + sp.l23 + sp.l5 + sp.l6;
+    const int NA = sp.n_columns * NPC;
+    Shard h;
+    h.rank = rank;
+    h.world = world;
+    h.c0 = (int)((int64_t)sp.n_columns * rank / world);
+    h.c1 = (int)((int64_t)sp.n_columns * (rank + 1) / world);
+    h.p0 = (int)((int64_t)sp.pf_groups * rank / world);
+    h.p1 = (int)((int64_t)sp.pf_groups * (rank + 1) / world);
+    h.a0 = h.c0 * NPC;
+    h.a1 = h.c1 * NPC;
+    h.pf0 = NA + h.p0 * sp.pf_group_size;
+    h.pf1 = NA + h.p1 * sp.pf_group_size;
+    return h;
+}
+
+void generate_reference(const snn_topology_spec& sp, HostNet& n, const Shard* shard) {
     SNN_REQUIRE(sp.n_columns >= 2 && sp.l4 > 0 && sp.l23 > 0 && sp.l5 > 0 && sp.l6 > 0 &&
                     sp.pf_groups > 0 && sp.pf_group_size > 0,
                 SNN_ERR_ARG, "stage2e topology: need >= 2 columns and non-empty layers");
@@ -85,25 +105,33 @@ void generate_reference(const snn_topology_spec& sp, HostNet& n) {
         if (deg[i] > 50) { deg[i]--; total--; }
     }
     SNN_REQUIRE(total < (int64_t)INT32_MAX, SNN_ERR_ARG, "synapse count exceeds int32 indexing");
-    n.S = total;
+    // generated rows: the reference's row pointer over all synapses
+    std::vector<int64_t> gen_ptr(N + 1, 0);
+    for (int i = 0; i < N; ++i) gen_ptr[i + 1] = gen_ptr[i] + deg[i];
+    const bool filter = shard && shard->world > 1;
+    const size_t cap = filter ? (size_t)(total / shard->world + total / (4 * shard->world) + 4096)
+                              : (size_t)total;
     n.row_ptr.assign(N + 1, 0);
-    for (int i = 0; i < N; ++i) n.row_ptr[i + 1] = n.row_ptr[i] + deg[i];
-    n.post.resize(total); n.delay.resize(total); n.flags.resize(total);
-    n.w0.resize(total); n.alpha.resize(total); n.beta.resize(total); n.u0.resize(total);
+    n.post.clear(); n.delay.clear(); n.flags.clear();
+    n.w0.clear(); n.alpha.clear(); n.beta.clear(); n.u0.clear();
+    n.post.reserve(cap);
+    n.delay.reserve(cap); n.flags.reserve(cap);
+    n.w0.reserve(cap); n.alpha.reserve(cap); n.beta.reserve(cap); n.u0.reserve(cap);
 
     const float w_scale = pm_div(2.0f, sqrtf(200.0f));
-    auto put = [&](int64_t k, int post, float w, int d, bool exc, bool ff) {
-        n.post[k] = post;
-        n.delay[k] = (uint8_t)d;
-        n.w0[k] = w;
+    auto put = [&](int64_t, int post, float w, int d, bool exc, bool ff) {
+        if (filter && !shard->owns(post)) return;
+        n.post.push_back(post);
+        n.delay.push_back((uint8_t)d);
+        n.w0.push_back(w);
         uint8_t f = exc ? (RF_AMPA | RF_NMDA) : (RF_GABA_A | RF_GABA_B);
         if (ff) f |= RF_FF;
-        n.flags[k] = f;
-        n.u0[k] = ff ? 0.02f : (exc ? 0.2f : 0.05f);
+        n.flags.push_back(f);
+        n.u0.push_back(ff ? 0.02f : (exc ? 0.2f : 0.05f));
         float r = pm_div(fabsf(w), 1.5f);
         if (r > 0.999f) r = 0.999f;
-        n.alpha[k] = pm_mul(r, 0.1f);
-        n.beta[k] = pm_mul(pm_sub(1.0f, r), 0.1f);
+        n.alpha.push_back(pm_mul(r, 0.1f));
+        n.beta.push_back(pm_mul(pm_sub(1.0f, r), 0.1f));
     };
     // flow rules L4->L2/3, L2/3->{L2/3,L5}, L5->{L6,L2/3}, L6->{L4,L6}
     auto target_layer = [&](int L) -> int {
@@ -115,8 +143,8 @@ void generate_reference(const snn_topology_spec& sp, HostNet& n) {
         }
     };
     for (int pre = 0; pre < N; ++pre) {
-        int64_t k = n.row_ptr[pre];
-        const int64_t kend = n.row_ptr[pre + 1];
+        int64_t k = gen_ptr[pre];
+        const int64_t kend = gen_ptr[pre + 1];
         const bool pf = pre >= NA;
         const int col = pf ? -1 : pre / NPC;
         const int L = pf ? (int)PF : layer_of(pre % NPC);
@@ -165,7 +193,9 @@ void generate_reference(const snn_topology_spec& sp, HostNet& n) {
             put(k++, post, w, d, exc, false);
         }
         while (k < kend) intra(true);
+        n.row_ptr[pre + 1] = (int32_t)n.post.size();
     }
+    n.S = (int64_t)n.post.size();
 }
 
 void build_layout(const HostNet& net, Layout& lay) {

@@ -24,8 +24,26 @@ struct HostNet {
     std::vector<int32_t> column;
 };
 
-// Reference rules (src/stage2e/network_init.cu:38-127, 158-473).
-void generate_reference(const snn_topology_spec& spec, HostNet& net);
+// Column sharding: rank r of `world` owns the columns [c0, c1) and the
+// prefrontal groups [p0, p1) (even split), i.e. the neurons [a0, a1) and
+// [pf0, pf1); its local neuron order is the first range, then the second.
+struct Shard {
+    int rank = 0, world = 1;
+    int c0 = 0, c1 = 0, p0 = 0, p1 = 0;
+    int a0 = 0, a1 = 0, pf0 = 0, pf1 = 0;
+    int n_local() const { return (a1 - a0) + (pf1 - pf0); }
+    bool owns(int g) const { return (g >= a0 && g < a1) || (g >= pf0 && g < pf1); }
+    int local_of(int g) const { return g < a1 ? g - a0 : (a1 - a0) + (g - pf0); }
+    int global_of(int j) const { return j < a1 - a0 ? a0 + j : pf0 + (j - (a1 - a0)); }
+};
+Shard make_shard(const snn_topology_spec& spec, int rank, int world);
+
+// Reference rules (src/stage2e/network_init.cu:38-127, 158-473).  With a
+// shard, the full random sequence is drawn but only the synapses onto the
+// shard's neurons are kept (in generation order, so that the canonical
+// ascending-id order of every kept neuron's incoming list is unchanged);
+// row_ptr then spans all N pres over the kept synapses.
+void generate_reference(const snn_topology_spec& spec, HostNet& net, const Shard* shard = nullptr);
 
 // Group / post-major layout.
 //   group  = distinct (pre, effective delay, feed-forward flag) of a pre's

@@ -97,7 +97,8 @@ EXPORTS = ["snn_config_init", "snn_topology_init", "snn_create", "snn_destroy",
            "snn_last_error", "snn_version", "snn_build_columns", "snn_set_corpus", "snn_step",
            "snn_run", "snn_synchronize", "snn_get_spikes", "snn_get_state", "snn_get_counters",
            "snn_set_dopamine", "snn_set_e0", "snn_save", "snn_load", "snn_stream_generate",
-           "snn_set_profiling", "snn_get_profile", "snn_propagate", "snn_propagate_static"]
+           "snn_set_profiling", "snn_get_profile", "snn_propagate", "snn_propagate_static",
+           "snn_nccl_unique_id", "snn_set_shard", "snn_shard_plan"]
 
 _lib = None
 
@@ -135,6 +136,9 @@ def lib():
         L.snn_get_profile.argtypes = [vp, C.POINTER(Profile)]
         L.snn_propagate.argtypes = [vp, vp, C.c_int64, C.c_int32, vp, vp, C.c_int64, C.c_int32, vp]
         L.snn_propagate_static.argtypes = L.snn_propagate.argtypes
+        L.snn_nccl_unique_id.argtypes = [vp, C.c_int64]
+        L.snn_set_shard.argtypes = [vp, C.c_int32, C.c_int32, vp, C.c_int64]
+        L.snn_shard_plan.argtypes = [C.POINTER(TopologySpec), C.c_int32, C.c_int32, vp, C.c_int32]
         _lib = L
     return _lib
 
@@ -154,6 +158,27 @@ def propagate(post, w, fanout, spikes, acc, frac_bits=24, stream=None, static=Fa
             acc.data_ptr(), acc.numel(), frac_bits, st.cuda_stream)
     if rc:
         raise SnnError(rc, lib().snn_last_error(None).decode())
+
+
+def nccl_unique_id():
+    """128-byte NCCL unique id (bytes) for snn_set_shard; make it on one rank
+    and share it with the others."""
+    buf = (C.c_uint8 * 128)()
+    rc = lib().snn_nccl_unique_id(buf, 128)
+    if rc:
+        raise SnnError(rc, lib().snn_last_error(None).decode())
+    return bytes(buf)
+
+
+def shard_plan(spec, rank, world):
+    """Host-only partition plan of a Stage 2e topology (no GPU needed)."""
+    out = np.zeros(10, np.int64)
+    rc = lib().snn_shard_plan(C.byref(spec), rank, world, out.ctypes.data, 10)
+    if rc:
+        raise SnnError(rc, lib().snn_last_error(None).decode())
+    keys = ["n_local", "a0", "a1", "pf0", "pf1", "synapses", "groups_local", "groups_mirror",
+            "mirror_pres", "remote_short_delay"]
+    return {k: int(v) for k, v in zip(keys, out)}
 
 
 def stream(n, seed=42, p_cjk=0.452, zipf_s=1.1):
@@ -288,6 +313,12 @@ class Network:
         p = Profile()
         self._check(self.L.snn_get_profile(self.h, C.byref(p)))
         return p.as_dict()
+
+    def set_shard(self, rank, world, uid=None):
+        """Column sharding (before build_columns): rank of world, NCCL id."""
+        b = (C.c_uint8 * 128).from_buffer_copy(uid) if uid is not None else None
+        self._check(self.L.snn_set_shard(self.h, rank, world, b, 128 if b is not None else 0))
+        self.rank, self.world = rank, world
 
     def set_dopamine(self, level):
         self._check(self.L.snn_set_dopamine(self.h, level))
