@@ -274,6 +274,96 @@ def prop_main(args):
             net.close()
 
 
+def shard_main(args):
+    """Configuration 3: the Stage 2e network scaled to --columns columns
+    (5,000: 5.5 M neurons / 1.07 B synapses), sharded by column over the
+    torchrun ranks (one GPU each), NCCL all-gather of the spike bitmask every
+    step.  Strong scaling: the network is the same at every rank count."""
+    import datetime
+    import torch
+    import torch.distributed as tdist
+    import snn_b200 as snn
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    warm = max(args.warmup, 3)
+    if world > 1:
+        tdist.init_process_group("gloo", timeout=datetime.timedelta(seconds=900))
+    torch.cuda.set_device(local)
+    uid = [snn.nccl_unique_id() if rank == 0 else None]
+    if world > 1:
+        tdist.broadcast_object_list(uid, src=0)
+    t_build = time.perf_counter()
+    net = snn.Network(device=local, phase_offset=PHASE_OFFSET, raster_steps=256)
+    net.set_shard(rank, world, uid[0] if world > 1 else None)
+    net.build_columns(snn.topology(n_columns=args.columns))
+    net.set_corpus(snn.stream(1 << 20, seed=STREAM_SEED, p_cjk=P_CJK))
+    build_s = time.perf_counter() - t_build
+    net.run(warm)
+    net.synchronize()
+    c0 = net.counters()
+    if world > 1:
+        tdist.barrier()
+    net.set_profiling(True)
+    with ClockSampler(local) as clk:
+        net.run(args.steps)
+        net.synchronize()
+    prof = net.profile()
+    net.set_profiling(False)
+    c1 = net.counters()
+    arr = float(c1["arrivals"] - c0["arrivals"])
+    dev_ms = prof["step_ms"]
+    # e2e: snn_run with the rank's raster rows copied to pinned host memory
+    e2e_steps = min(args.e2e_steps, 200)
+    raster = torch.empty((e2e_steps, net.words), dtype=torch.int32, pin_memory=True)
+    net.run(50)  # untimed: re-instantiates the step graph after profiling
+    net.synchronize()
+    ce0 = net.counters()
+    if world > 1:
+        tdist.barrier()
+    t0 = time.perf_counter()
+    net._check(net.L.snn_run(net.h, e2e_steps, None, 0, 1, raster.data_ptr(), None))
+    net.synchronize()
+    wall = time.perf_counter() - t0
+    e2e_arr = float(net.counters()["arrivals"] - ce0["arrivals"])
+    v = torch.tensor([dev_ms, wall, build_s], dtype=torch.float64)
+    e = torch.tensor([arr, e2e_arr, float(net.S)], dtype=torch.float64)
+    if world > 1:
+        tdist.all_reduce(v, op=tdist.ReduceOp.MAX)
+        tdist.all_reduce(e, op=tdist.ReduceOp.SUM)
+    dev_ms, wall, build_s = (float(x) for x in v)
+    arr_all, e2e_all, syn_all = (float(x) for x in e)
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        line = {
+            "metric": "synaptic events/sec (SOPS) and sim steps/sec, Stage-2e 5.5M/1.07B column-sharded",
+            "value": arr_all / (dev_ms / 1000.0), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": warm, "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded UTF-8 stream, ref45 preset)",
+            "steps_per_sec": args.steps / (dev_ms / 1000.0),
+            "config": {"workload": f"stage2e {args.columns:,} columns ({args.columns * 1100:,} neurons / "
+                                   f"{int(syn_all):,} synapses), column-sharded over {world} GPU(s), "
+                                   "SYNAPTOGENIC phase",
+                       "columns": args.columns, "parallelism": f"column shards x{world}",
+                       "exchange": "NCCL all-gather of spike words + counts every step",
+                       "events_per_step": arr_all / args.steps, "build_s": build_s,
+                       "l2": "inputs larger than L2"},
+            "e2e": {"value": e2e_all / wall, "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": net.words * 4},
+            "gpu_launches": int(sum(k["launches"] for n, k in prof["kernels"].items() if "@" not in n)),
+            "kernels_ms_per_step_rank0": {k: x["ms"] / max(x["launches"], 1)
+                                          for k, x in prof["kernels"].items()},
+            "clocks": clk.summary(),
+            "peak_hbm_gbs": peak, "peak_kind": peak_kind,
+        }
+        print(json.dumps(line), flush=True)
+    net.close()
+    if world > 1:
+        tdist.barrier()
+        tdist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -282,9 +372,11 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=1000)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="stage2e", choices=["stage2e", "prop"],
+    ap.add_argument("--workload", default="stage2e", choices=["stage2e", "prop", "shard"],
                     help="stage2e: the 55k/10.7M network (one line); prop: the 1M x 1,000 "
-                         "propagation microbench (one line per mode and rate, 1 GPU)")
+                         "propagation microbench (one line per mode and rate, 1 GPU); shard: "
+                         "the 100x network column-sharded over the torchrun ranks")
+    ap.add_argument("--columns", type=int, default=5000, help="shard workload: columns")
     ap.add_argument("--prop-neurons", type=int, default=1_000_000)
     ap.add_argument("--prop-rates", default="", help="comma list, default 0.001,0.01,0.03,0.1")
     ap.add_argument("--prop-modes", default="", help="comma list of 0 (STDP off), 1 (STDP on), 2 (STP on)")
@@ -292,6 +384,9 @@ def main():
     warm = max(args.warmup, 3)
     if args.workload == "prop":
         prop_main(args)
+        return
+    if args.workload == "shard":
+        shard_main(args)
         return
 
     rank = int(os.environ.get("RANK", "0"))

@@ -137,6 +137,7 @@ struct Dev {
     // groups of remote pres ("mirror" groups, after the local ones) are
     // updated by k_mirror from the gathered bits.
     int n_a, a0, pf0, sharded, world;
+    int c0, c1;             // this rank's columns
     unsigned* send;
     const unsigned* recv;
     int pw, words_max;      // payload words per rank; count word index
@@ -164,7 +165,8 @@ __device__ __forceinline__ float clampf(float x, float lo, float hi) {
 // the thalamic gate from the column counts of step t-1
 // (src/stage2e/thalamic_gate.cu:53-142).
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(64) k_control(Dev d, Consts k) {
+constexpr int CTL_THREADS = 512;  // the column loops cover up to thousands of columns
+__global__ void __launch_bounds__(CTL_THREADS) k_control(Dev d, Consts k) {
     Ctrl* c = d.ctrl;
     __shared__ long long s_t;
     __shared__ int s_inject, s_byte;
@@ -217,14 +219,15 @@ __global__ void __launch_bounds__(64) k_control(Dev d, Consts k) {
     __syncthreads();
     const long long t = s_t;
     const bool prev_ok = t > 0;
-    for (int q = tid; q < d.ncol; q += blockDim.x) {
+    // this rank's columns [c0, c1) (all columns unsharded)
+    for (int q = d.c0 + tid; q < d.c1; q += blockDim.x) {
         d.col_sp[(t & 1) * d.ncol + q] = 0;
         d.l6_sp[(t & 1) * d.ncol + q] = 0;
     }
     for (int q = tid; q < TD_DIM; q += blockDim.x) d.sub_sp[(t & 1) * TD_DIM + q] = 0;
     if (d.sharded)
         for (int q = tid; q < 1 + TD_DIM; q += blockDim.x) d.send[d.words_max + q] = 0u;
-    for (int col = tid; col < d.ncol; col += blockDim.x) {
+    for (int col = d.c0 + tid; col < d.c1; col += blockDim.x) {
         float4 g = d.gates[col];
         const float cur = prev_ok ? pm_i2f(d.col_sp[((t - 1) & 1) * d.ncol + col]) : 0.0f;
         const float l6c = prev_ok ? pm_i2f(d.l6_sp[((t - 1) & 1) * d.ncol + col]) : 0.0f;
@@ -1067,7 +1070,7 @@ struct Engine2e : snnb::Engine {
         D.N = N; D.N_assoc = net.N_assoc; D.NPC = net.NPC; D.ncol = net.ncol; D.l4 = net.l4;
         D.per_sub = NG / TD_DIM;
         SNN_REQUIRE(D.per_sub > 0, SNN_ERR_ARG, "network too small for the 200-dim value function");
-        D.n_a = sh.a1 - sh.a0; D.a0 = sh.a0; D.pf0 = sh.pf0;
+        D.n_a = sh.a1 - sh.a0; D.a0 = sh.a0; D.pf0 = sh.pf0; D.c0 = sh.c0; D.c1 = sh.c1;
         D.sharded = world > 1 ? 1 : 0;
         D.world = world;
         D.words = (N + 31) / 32;
@@ -1281,7 +1284,7 @@ struct Engine2e : snnb::Engine {
         const unsigned fl = capturing ? cudaEventRecordExternal : cudaEventRecordDefault;
         int e = 0;
         if (ev) SNN_CUDA(cudaEventRecordWithFlags(ev[e++], st, fl));
-        k_control<<<1, 64, 0, st>>>(D, K);
+        k_control<<<1, CTL_THREADS, 0, st>>>(D, K);
         if (ev) SNN_CUDA(cudaEventRecordWithFlags(ev[e++], st, fl));
         k_neurons<<<nb, NEU_BLOCK, 0, st>>>(D, K);
         if (ev) SNN_CUDA(cudaEventRecordWithFlags(ev[e++], st, fl));
