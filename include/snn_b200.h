@@ -171,6 +171,8 @@ enum {
     SNN_STATE_CAMKII_AUTO = 30,/* f32[S]                                    */
     SNN_STATE_E1 = 31,         /* f32[S]                                    */
     SNN_STATE_E2 = 32,         /* f32[S]                                    */
+    SNN_STATE_AMPA = 33,       /* f32[S] AMPA conductance (Stage 2e)        */
+    SNN_STATE_LAST_PRE = 34,   /* f32[S] step of the last arrival (Stage 2e) */
     SNN_STATE_POST = 40,       /* i32[S] post neuron of each synapse        */
     SNN_STATE_DELAY = 41,      /* u8[S]                                     */
     SNN_STATE_ROW_PTR = 42,    /* i32[N+1] pre-major CSR row pointer        */

@@ -1003,7 +1003,7 @@ void o2e_spikes(void* h, uint8_t* out) {
 }
 // synapse field export, pre-major order; which: 0 alpha, 1 beta, 2 weight, 3 x_pre,
 // 4 x_post, 5 nmda, 6 ca, 7 R, 8 u, 9 elig, 10 camkii_act, 11 autophos, 12 e1, 13 e2,
-// 14 ampa
+// 14 ampa, 15 last_pre
 void o2e_synapse_f32(void* h, int32_t which, float* out) {
     Oracle* o = (Oracle*)h;
     for (long long i = 0; i < o->S; ++i) {
@@ -1025,10 +1025,29 @@ void o2e_synapse_f32(void* h, int32_t which, float* out) {
             case 12: v = o->e1[i]; break;
             case 13: v = o->e2[i]; break;
             case 14: v = s.ampa; break;
+            case 15: v = s.last_pre; break;
         }
         out[i] = v;
     }
 }
+// SCKP v2 file as BioMechanismScheduler::save_checkpoint writes it
+// (src/stage2e/scheduler.cu:411-483): u32 magic 0x53434B50, u32 version 2,
+// u32 step, u32 n_syn, u32 n_neu, BioSynapse[n_syn] (80 B each, the Syn
+// layout above), i32 neuron_byte_counts[n_neu * 256], f32 alpha[n_syn],
+// f32 beta[n_syn].  Returns 0, or 2 when the file cannot be written.
+int o2e_save_sckp(void* h, const char* path, int32_t step) {
+    Oracle* o = (Oracle*)h;
+    FILE* fp = fopen(path, "wb");
+    if (!fp) return 2;
+    const uint32_t hdr[5] = {0x53434B50u, 2u, (uint32_t)step, (uint32_t)o->S, (uint32_t)o->N};
+    fwrite(hdr, sizeof(uint32_t), 5, fp);
+    fwrite(o->syn.data(), sizeof(Syn), (size_t)o->S, fp);
+    fwrite(o->neuron_byte_counts.data(), sizeof(int32_t), (size_t)o->N * 256, fp);
+    fwrite(o->alpha.data(), sizeof(float), (size_t)o->S, fp);
+    fwrite(o->beta.data(), sizeof(float), (size_t)o->S, fp);
+    return fclose(fp) == 0 ? 0 : 2;
+}
+
 // control-state export: gates[4*n_columns], modulators[4], byte_histogram[256]
 void o2e_control(void* h, float* gates, float* mods, int32_t* byte_hist) {
     Oracle* o = (Oracle*)h;

@@ -38,7 +38,7 @@ class O2eCounters(C.Structure):
 
 SYN_FIELDS = {"alpha": 0, "beta": 1, "weight": 2, "x_pre": 3, "x_post": 4, "nmda": 5,
               "ca": 6, "R": 7, "u": 8, "elig": 9, "camkii_act": 10, "autophos": 11,
-              "e1": 12, "e2": 13, "ampa": 14}
+              "e1": 12, "e2": 13, "ampa": 14, "last_pre": 15}
 NEU_FIELDS = {"V": 0, "s": 1, "w": 2, "fr": 3, "ca": 4, "input": 5, "nmda_cur": 6,
               "inh": 7, "spike": 8, "last": 9, "ref": 10}
 
@@ -156,6 +156,14 @@ class Oracle2e:
         out = np.zeros(self.S, np.float32)
         self.L.o2e_synapse_f32(self.h, SYN_FIELDS[name], out.ctypes.data)
         return out
+
+    def save_sckp(self, path, step):
+        """SCKP v2 file of the current state (the reference scheduler's layout)."""
+        L = lib()
+        L.o2e_save_sckp.argtypes = [C.c_void_p, C.c_char_p, C.c_int32]
+        rc = L.o2e_save_sckp(self.h, path.encode(), step)
+        if rc:
+            raise OSError(f"o2e_save_sckp failed ({rc})")
 
     def control(self):
         g = np.zeros(4 * self.p.n_columns, np.float32)

@@ -18,6 +18,7 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
+#include "ckpt.h"
 #include "common.h"
 #include "snn_pmath.h"
 
@@ -582,8 +583,149 @@ struct Engine0 : snnb::Engine {
     }
     void get_profile(snn_profile* o) override { *o = prof; }
 
-    void save(const char*, int32_t) override { throw snnb::Error(SNN_ERR_UNSUPPORTED, "stage0 save not implemented yet"); }
-    void load(const char*, int32_t) override { throw snnb::Error(SNN_ERR_UNSUPPORTED, "stage0 load not implemented yet"); }
+    // ---- checkpoints ------------------------------------------------------
+    // Device synapse order is the reference CSR order (incoming synapses by
+    // post), the order of its d_synapses_ / d_col_idx_ / d_weights_ arrays.
+    struct NativeBlob {
+        int64_t steps, raster_base, corpus_pos, corpus_len, N, S;
+        float dopamine;
+        int32_t raster_cap, preset, ncol;
+    };
+    NativeBlob blob() const {
+        NativeBlob b{};
+        b.steps = steps; b.raster_base = raster_base_host; b.corpus_pos = corpus_pos;
+        b.corpus_len = corpus_len; b.N = N; b.S = S; b.dopamine = dopamine;
+        b.raster_cap = raster_cap; b.preset = cfg.preset; b.ncol = ncol;
+        return b;
+    }
+    std::vector<snnb::DevSection> native_sections() {
+        std::vector<snnb::DevSection> v;
+        auto add = [&](const char* n, auto& b) { v.push_back({n, (void*)b.p, b.bytes()}); };
+        add("V", V); add("I", I); add("fr", fr); add("A", A); add("B", B); add("input", input);
+        add("w", w); add("e", e); add("ref", ref); add("last", last); add("off", off); add("spk", spk);
+        add("raster", raster); add("ctrl", ctrl);
+        return v;
+    }
+    // SNN2 v1 (src/stage2/unsupervised_trainer.cu:176-262): u32 magic
+    // 0x534E4E32, u32 version 1, i64 step, u64 text_pos, i32 n_neurons,
+    // i32 n_synapses, Synapse[n] {pre, post, w, delay, last_pre, last_post,
+    // eligibility, pad} (32 B), i32 row_ptr[N+1], i32 col_idx[S], f32 w[S]
+    struct Syn32 {
+        int32_t pre, post;
+        float w, delay, last_pre, last_post, elig, pad;
+    };
+    static_assert(sizeof(Syn32) == 32, "Synapse record");
+    void save(const char* path, int32_t fmt) override {
+        SNN_REQUIRE(built, SNN_ERR_STATE, "build the network first");
+        SNN_CUDA(cudaStreamSynchronize(stream));
+        if (fmt == SNN_FMT_NATIVE) {
+            const NativeBlob b = blob();
+            snnb::save_native(path, SNN_MODEL_STAGE0, &b, sizeof(b), native_sections(), stream);
+            return;
+        }
+        if (fmt == SNN_FMT_RAW_F32) {  // src/host/network.cpp:224-246
+            snnb::BinFile f(path, true);
+            f.put_dev(w.p, (size_t)S * 4, stream);
+            f.close();
+            return;
+        }
+        SNN_REQUIRE(fmt == SNN_FMT_SNN2_V1, SNN_ERR_UNSUPPORTED,
+                    "Stage 0 writes the native, SNN2 v1 and raw formats");
+        std::vector<float> hw((size_t)S), he((size_t)S), hA((size_t)N);
+        std::vector<unsigned> hp((size_t)S);
+        w.download(hw.data(), S, stream);
+        e.download(he.data(), S, stream);
+        A.download(hA.data(), N, stream);
+        pre.download(hp.data(), S, stream);
+        SNN_CUDA(cudaStreamSynchronize(stream));
+        std::vector<Syn32> aos((size_t)S);
+        std::vector<int32_t> col((size_t)S);
+        for (int j = 0; j < N; ++j)
+            for (int32_t p = in_ptr_h[j]; p < in_ptr_h[j + 1]; ++p) {
+                const int32_t q = (int32_t)(hp[p] & 0x7fffffffu);
+                aos[p] = Syn32{q, j, hw[p], 1.0f, hA[q], hA[j], he[p], 0.0f};
+                col[p] = q;
+            }
+        snnb::BinFile f(path, true);
+        f.put_v<uint32_t>(0x534E4E32u);
+        f.put_v<uint32_t>(1u);
+        f.put_v<int64_t>(steps);
+        f.put_v<uint64_t>((uint64_t)corpus_pos);
+        f.put_v<int32_t>(N);
+        f.put_v<int32_t>((int32_t)S);
+        f.put(aos.data(), sizeof(Syn32) * aos.size());
+        f.put(in_ptr_h.data(), 4 * (size_t)(N + 1));
+        f.put(col.data(), 4 * col.size());
+        f.put(hw.data(), 4 * hw.size());
+        f.close();
+    }
+    void load(const char* path, int32_t fmt) override {
+        SNN_REQUIRE(built, SNN_ERR_STATE, "build the network first");
+        SNN_CUDA(cudaStreamSynchronize(stream));
+        if (fmt == SNN_FMT_NATIVE) {
+            const NativeBlob want = blob();
+            NativeBlob got{};
+            snnb::load_native(path, SNN_MODEL_STAGE0, &got, sizeof(got), native_sections(), stream,
+                              [&](const void* p) {
+                                  NativeBlob f;
+                                  memcpy(&f, p, sizeof(f));
+                                  SNN_REQUIRE(f.N == want.N && f.S == want.S && f.raster_cap == want.raster_cap &&
+                                                  f.preset == want.preset && f.ncol == want.ncol,
+                                              SNN_ERR_IO, "checkpoint of another network");
+                              });
+            steps = got.steps; raster_base_host = got.raster_base; corpus_pos = got.corpus_pos;
+            dopamine = got.dopamine;
+            SNN_REQUIRE(got.corpus_len == corpus_len, SNN_ERR_IO,
+                        "set the checkpoint's corpus (same length) before loading it");
+            return;
+        }
+        if (fmt == SNN_FMT_RAW_F32) {  // src/host/network.cpp:248-290: exactly S floats
+            snnb::BinFile f(path, false);
+            SNN_REQUIRE(f.size() == S * 4, SNN_ERR_IO, "raw weight file size differs from the network");
+            f.get_dev(w.p, (size_t)S * 4, stream);
+            return;
+        }
+        SNN_REQUIRE(fmt == SNN_FMT_SNN2_V1, SNN_ERR_UNSUPPORTED,
+                    "Stage 0 reads the native, SNN2 v1 and raw formats");
+        // src/stage2/unsupervised_trainer.cu:264-348: header, sizes, then the
+        // synapse records (their weight, eligibility and spike times); the
+        // CSR must be this network's
+        snnb::BinFile f(path, false);
+        SNN_REQUIRE(f.size() >= 32, SNN_ERR_IO, "truncated SNN2 file");
+        SNN_REQUIRE(f.get_v<uint32_t>() == 0x534E4E32u, SNN_ERR_IO, "not an SNN2 file (bad magic)");
+        SNN_REQUIRE(f.get_v<uint32_t>() == 1u, SNN_ERR_IO, "SNN2 version differs");
+        const int64_t step = f.get_v<int64_t>();
+        const uint64_t pos = f.get_v<uint64_t>();
+        const int32_t nn = f.get_v<int32_t>(), ns = f.get_v<int32_t>();
+        SNN_REQUIRE(nn == N && ns == (int32_t)S, SNN_ERR_IO, "SNN2 sizes differ from this network");
+        SNN_REQUIRE(f.size() == 32 + 32 * S + 4 * (int64_t)(N + 1) + 8 * S, SNN_ERR_IO, "truncated SNN2 file");
+        std::vector<Syn32> aos((size_t)S);
+        f.get(aos.data(), sizeof(Syn32) * aos.size());
+        std::vector<int32_t> rp((size_t)N + 1), col((size_t)S);
+        f.get(rp.data(), 4 * rp.size());
+        f.get(col.data(), 4 * col.size());
+        std::vector<unsigned> hp((size_t)S);
+        pre.download(hp.data(), S, stream);
+        SNN_CUDA(cudaStreamSynchronize(stream));
+        SNN_REQUIRE(rp == in_ptr_h, SNN_ERR_IO, "SNN2 row pointer differs from this network");
+        for (int64_t p = 0; p < S; ++p)
+            SNN_REQUIRE(col[p] == (int32_t)(hp[p] & 0x7fffffffu), SNN_ERR_IO,
+                        "SNN2 column index differs from this network");
+        std::vector<float> hw((size_t)S), he((size_t)S), hA((size_t)N, -1000.0f);
+        for (int64_t p = 0; p < S; ++p) {
+            hw[p] = aos[p].w;
+            he[p] = aos[p].elig;
+            hA[aos[p].pre] = aos[p].last_pre;
+            hA[aos[p].post] = aos[p].last_post;
+        }
+        w.upload(hw.data(), S, stream);
+        e.upload(he.data(), S, stream);
+        A.upload(hA.data(), N, stream);
+        B.upload(hA.data(), N, stream);  // only read within a spiking step, after it is set
+        SNN_CUDA(cudaStreamSynchronize(stream));
+        steps = step;
+        corpus_pos = corpus_len > 0 ? (long long)(pos % (uint64_t)corpus_len) : 0;
+    }
 };
 
 }  // namespace snn0

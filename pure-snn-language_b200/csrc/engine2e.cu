@@ -1,11 +1,10 @@
 // engine2e.cu - Stage 2e engine on sm_100a: AdEx neurons, NMDA/Ca synapses,
 // Tsodyks-Markram STP, dual-trace PSW STDP, CaMKII / eligibility, axonal
-// delays, thalamic gate, modulators and inhibition, one step = 3 kernels:
+// delays, thalamic gate, modulators and inhibition, one step = 2 kernels
+// (+ the all-gather and k_mirror between them on column shards):
 //
-//   k_control   (1 CTA)     deferred control of step t-1 (inhibition drive,
-//                           modulators / TD value function, statistics),
-//                           thalamic gate, byte, phase gain, M_ij of step t
-//   k_neurons   (N threads) population-coded input, inhibition, AdEx update,
+//   k_neurons   (N threads) start of step t (byte, phase gain, M_ij, thalamic
+//                           gates), population-coded input, inhibition, AdEx update,
 //                           spike history / raster / counters, Mg block and
 //                           post trace of the neuron, then the update of the
 //                           neuron's outgoing synapse groups (NMDA g, pre
@@ -14,7 +13,10 @@
 //                           synapses: Ca / NMDA current, LTP (post spike),
 //                           LTD (arrival), dispatch value capture, input
 //                           current for the next step, CaMKII / eligibility
-//                           fold every 10 steps, PSW decay every 1000 steps
+//                           fold every 10 steps, PSW decay every 1000 steps;
+//                           CTA 0 first runs the end of step t (inhibition
+//                           drive, modulators / TD value function, statistics,
+//                           hand-over of byte history and counters to t + 1)
 //
 // Semantics follow src/stage2e/scheduler.cu:485-676 step for step; the CPU
 // oracle (oracle/oracle2e.cpp) states the same semantics with per-synapse
@@ -38,6 +40,7 @@
 #include <cstdio>
 #include <memory>
 #include <nccl.h>
+#include "ckpt.h"
 #include "common.h"
 #include "net2e.h"
 #include "snn_pmath.h"
@@ -63,7 +66,7 @@ struct Consts {
     float ca_n_inc, ca_n_dec, fr_refr, fr_spk_keep, fr_spk_add, fr_quiet, off_decay;
     int refr_steps, off_add, off_max;
     // synapse
-    float dec_nmda, dec_ca, dec_ca_ff, ca_max, ca_max_ff, rec_ff_step, dec_xpre, dec_xpost;
+    float dec_nmda, dec_ampa, dec_ca, dec_ca_ff, ca_max, ca_max_ff, rec_ff_step, dec_xpre, dec_xpost;
     float g_nmda, ca_gain, e_rev, i_gain, i_min;
     float U[NCLASS], fac[NCLASS], rec[NCLASS];
     float a_plus, a_minus, w_max, eta, eta_ff, reb_thr, reb_gain, ab_min, ab_reset, psw_decay;
@@ -110,6 +113,7 @@ struct Dev {
     float4* gstate;  // R, u, nmda, xpre
     float2* gview;   // hot view of step t: nmda, flags (as bits)
     float2* gcold;   // cold view of step t: xpre before the arrival jump, R after STP
+    float2* gextra;  // AMPA conductance, step of the last arrival (checkpoint fields)
     // synapses (post-major)
     unsigned* gid;
     float* ca;
@@ -118,7 +122,7 @@ struct Dev {
     float* val;      // VAL_SLOTS per synapse
     // control
     Ctrl* ctrl;
-    float4* gates;   // gate, act_ema, nov_ema, l6_ema
+    float4* gates;   // [2][ncol] gate, act_ema, nov_ema, l6_ema after even / odd steps
     int *col_sp, *l6_sp, *sub_sp;  // [2][ncol], [2][ncol], [2][TD_DIM]
     unsigned* byte_hist_nov;
     int* byte_histogram;
@@ -160,104 +164,89 @@ __device__ __forceinline__ float clampf(float x, float lo, float hi) {
 }
 
 // ---------------------------------------------------------------------------
-// k_control: one CTA at the start of step t.  Phase gain, byte and M_ij of
-// step t (src/stage2e/scheduler.cu:485-540, synapse_kernels.cu:207-211) and
-// the thalamic gate from the column counts of step t-1
-// (src/stage2e/thalamic_gate.cu:53-142).
+// Start of step t (src/stage2e/scheduler.cu:485-540, synapse_kernels.cu:
+// 207-211, thalamic_gate.cu:53-142), computed at the top of k_neurons: every
+// CTA derives t, the injection flag and the byte itself (the same function of
+// the control block, which nothing modifies until the step's epilogue), CTA 0
+// also publishes phase gain, pruning threshold and M_ij for the synapse pass,
+// and the thalamic gates are stepped by the CTAs that hold L4 neurons of a
+// column (each computes the same value from the gate state of step t-1; the
+// CTA holding the column's first neuron stores it).
 // ---------------------------------------------------------------------------
-constexpr int CTL_THREADS = 512;  // the column loops cover up to thousands of columns
-__global__ void __launch_bounds__(CTL_THREADS) k_control(Dev d, Consts k) {
+struct StepIn {
+    long long t;
+    int inject, byte;
+};
+
+__device__ __forceinline__ StepIn step_inputs(const Dev& d, const Consts& k) {
+    const Ctrl* c = d.ctrl;
+    StepIn s;
+    s.t = c->next_t;
+    s.inject = (s.t % k.inject_interval) == 0;
+    s.byte = 0;
+    if (s.inject) {
+        const int bo = c->byte_override;
+        const long long clen = c->corpus_len;
+        if (bo >= 0) s.byte = bo;
+        else if (clen > 0) s.byte = d.corpus[c->corpus_pos];
+        else s.byte = (int)((s.t / k.inject_interval) % 256);
+    }
+    return s;
+}
+
+// CTA 0: per-step scalars of the synapse pass and the epilogue
+__device__ void publish_step(const Dev& d, const Consts& k, const StepIn& s) {
     Ctrl* c = d.ctrl;
-    __shared__ long long s_t;
-    __shared__ int s_inject, s_byte;
-    __shared__ unsigned s_total_h, s_bc;
-    const int tid = threadIdx.x;
-    if (tid == 0) {
-        // all loads first (independent), then the dependent byte lookups
-        const long long t = c->next_t;
-        const int phase_offset = c->phase_offset, learn = c->learn, bo = c->byte_override;
-        const int e0 = c->e0;
-        const long long clen = c->corpus_len, cpos = c->corpus_pos;
-        const float c0 = c->conc[0], c1 = c->conc[1], c2 = c->conc[2], c3 = c->conc[3];
-        const unsigned htot = c->hist_total;
-        const int inj = (t % k.inject_interval) == 0;
-        int byte = 0;
-        if (inj) {
-            if (bo >= 0) byte = bo;
-            else if (clen > 0) byte = d.corpus[cpos];
-            else byte = (int)((t / k.inject_interval) % 256);
-        }
-        const unsigned bc = d.byte_hist_nov[byte];
-        const int ph = phase_of(t + phase_offset);
-        float M[2];
-        for (int e = 0; e < 2; ++e) {
-            if (e0) { M[e] = 1.0f; continue; }
-            float z = pm_mul(k.rec_da[e], c0);
-            z = pm_fma(k.rec_ach, c1, z);
-            z = pm_fma(k.rec_ne, c2, z);
-            z = pm_fma(k.rec_ht5, c3, z);
-            M[e] = pm_div(1.0f, pm_add(1.0f, snn_expf(-z)));
-        }
-        c->t = t;
-        c->next_t = t + 1;
-        c->gain = learn ? c_phase_gain[ph] : 0.0f;
-        c->prune_thr = c_phase_prune[ph];
-        if (inj && bo < 0 && clen > 0) c->corpus_pos = (cpos + 1) % clen;
-        c->byte_override = -1;
-        c->inject = inj;
-        c->byte = inj ? byte : -1;
-        c->M[0] = M[0];
-        c->M[1] = M[1];
-        c->step_spikes[t & 1] = 0;
-        c->step_arrivals[t & 1] = 0ull;
-        s_t = t;
-        s_inject = inj;
-        s_byte = byte;
-        s_total_h = htot;
-        s_bc = bc;
+    const int ph = phase_of(s.t + c->phase_offset);
+    const int learn = c->learn, e0 = c->e0;
+    const float c0 = c->conc[0], c1 = c->conc[1], c2 = c->conc[2], c3 = c->conc[3];
+    float M[2];
+    for (int e = 0; e < 2; ++e) {
+        if (e0) { M[e] = 1.0f; continue; }
+        float z = pm_mul(k.rec_da[e], c0);
+        z = pm_fma(k.rec_ach, c1, z);
+        z = pm_fma(k.rec_ne, c2, z);
+        z = pm_fma(k.rec_ht5, c3, z);
+        M[e] = pm_div(1.0f, pm_add(1.0f, snn_expf(-z)));
     }
-    __syncthreads();
-    const long long t = s_t;
+    c->t = s.t;
+    c->gain = learn ? c_phase_gain[ph] : 0.0f;
+    c->prune_thr = c_phase_prune[ph];
+    c->inject = s.inject;
+    c->byte = s.inject ? s.byte : -1;
+    c->M[0] = M[0];
+    c->M[1] = M[1];
+}
+
+// thalamic gate of column `col` after step t (double-buffered by t & 1)
+__device__ float4 gate_step(const Dev& d, int col, const StepIn& s) {
+    const long long t = s.t;
+    float4 g = d.gates[((t + 1) & 1) * d.ncol + col];
     const bool prev_ok = t > 0;
-    // this rank's columns [c0, c1) (all columns unsharded)
-    for (int q = d.c0 + tid; q < d.c1; q += blockDim.x) {
-        d.col_sp[(t & 1) * d.ncol + q] = 0;
-        d.l6_sp[(t & 1) * d.ncol + q] = 0;
+    const float cur = prev_ok ? pm_i2f(d.col_sp[((t - 1) & 1) * d.ncol + col]) : 0.0f;
+    const float l6c = prev_ok ? pm_i2f(d.l6_sp[((t - 1) & 1) * d.ncol + col]) : 0.0f;
+    const float den = g.y > 1.0f ? g.y : 1.0f;
+    const float an = fminf(1.0f, fmaxf(-1.0f, pm_div(pm_sub(g.y, cur), den)));
+    const float l6d = g.w > 1.0f ? g.w : 1.0f;
+    const float l6n = fminf(1.0f, fmaxf(-1.0f, pm_div(pm_sub(g.w, l6c), l6d)));
+    float nov = 0.0f;
+    if (s.inject) {
+        const unsigned htot = d.ctrl->hist_total, bc = d.byte_hist_nov[s.byte];
+        const unsigned tm = htot > 1u ? htot : 1u;
+        nov = pm_sub(1.0f, pm_div(pm_u2f(bc), pm_u2f(tm)));
+        nov = fminf(1.0f, fmaxf(0.0f, nov));
     }
-    for (int q = tid; q < TD_DIM; q += blockDim.x) d.sub_sp[(t & 1) * TD_DIM + q] = 0;
-    if (d.sharded)
-        for (int q = tid; q < 1 + TD_DIM; q += blockDim.x) d.send[d.words_max + q] = 0u;
-    for (int col = d.c0 + tid; col < d.c1; col += blockDim.x) {
-        float4 g = d.gates[col];
-        const float cur = prev_ok ? pm_i2f(d.col_sp[((t - 1) & 1) * d.ncol + col]) : 0.0f;
-        const float l6c = prev_ok ? pm_i2f(d.l6_sp[((t - 1) & 1) * d.ncol + col]) : 0.0f;
-        const float den = g.y > 1.0f ? g.y : 1.0f;
-        const float an = fminf(1.0f, fmaxf(-1.0f, pm_div(pm_sub(g.y, cur), den)));
-        const float l6d = g.w > 1.0f ? g.w : 1.0f;
-        const float l6n = fminf(1.0f, fmaxf(-1.0f, pm_div(pm_sub(g.w, l6c), l6d)));
-        float nov = 0.0f;
-        if (s_inject) {
-            const unsigned tm = s_total_h > 1u ? s_total_h : 1u;
-            nov = pm_sub(1.0f, pm_div(pm_u2f(s_bc), pm_u2f(tm)));
-            nov = fminf(1.0f, fmaxf(0.0f, nov));
-        }
-        const float om99 = pm_sub(1.0f, 0.99f), om95 = pm_sub(1.0f, 0.95f);
-        g.y = pm_fma(0.99f, g.y, pm_mul(om99, cur));
-        g.w = pm_fma(0.99f, g.w, pm_mul(om99, l6c));
-        g.z = pm_fma(0.95f, g.z, pm_mul(om95, nov));
-        float tg = pm_fma(0.3f, an, 0.5f);
-        tg = pm_fma(0.2f, g.z, tg);
-        tg = pm_fma(0.15f, l6n, tg);
-        tg = fminf(0.9f, fmaxf(0.1f, tg));
-        g.x = pm_fma(0.01f, pm_sub(tg, g.x), g.x);
-        g.x = fminf(1.0f, fmaxf(0.0f, g.x));
-        d.gates[col] = g;
-    }
-    __syncthreads();
-    if (tid == 0 && s_inject) {
-        d.byte_hist_nov[s_byte] += (unsigned)d.ncol;
-        c->hist_total += (unsigned)d.ncol;
-    }
+    const float om99 = pm_sub(1.0f, 0.99f), om95 = pm_sub(1.0f, 0.95f);
+    g.y = pm_fma(0.99f, g.y, pm_mul(om99, cur));
+    g.w = pm_fma(0.99f, g.w, pm_mul(om99, l6c));
+    g.z = pm_fma(0.95f, g.z, pm_mul(om95, nov));
+    float tg = pm_fma(0.3f, an, 0.5f);
+    tg = pm_fma(0.2f, g.z, tg);
+    tg = pm_fma(0.15f, l6n, tg);
+    tg = fminf(0.9f, fmaxf(0.1f, tg));
+    g.x = pm_fma(0.01f, pm_sub(tg, g.x), g.x);
+    g.x = fminf(1.0f, fmaxf(0.0f, g.x));
+    return g;
 }
 
 // ---------------------------------------------------------------------------
@@ -323,19 +312,37 @@ __device__ void step_epilogue(const Dev& d, const Consts& k) {
     c->last_spikes = sp;
     const unsigned long long arr = c->step_arrivals[t & 1];
     if (arr > 750000ull) c->dropped_ref += arr - 750000ull;
+    // hand-over to step t + 1: what must follow every CTA of step t's k_neurons
+    if (c->inject) {
+        d.byte_hist_nov[c->byte] += (unsigned)d.ncol;
+        c->hist_total += (unsigned)d.ncol;
+        const long long clen = c->corpus_len;
+        if (c->byte_override < 0 && clen > 0) c->corpus_pos = (c->corpus_pos + 1) % clen;
+    }
+    c->byte_override = -1;
+    c->step_spikes[(t + 1) & 1] = 0;
+    c->step_arrivals[(t + 1) & 1] = 0ull;
+    c->next_t = t + 1;
 }
 
 // STP / NMDA / pre-trace update of group g at step t from its pre's spike
 // history h (bit 0 = spike at t, bit d = spike at t - d) and its per-step
 // view for the synapse pass
 __device__ __forceinline__ void update_group(const Dev& d, const Consts& k, int g, unsigned meta, float4 st,
-                                             unsigned h, unsigned long long& arr_cnt,
+                                             unsigned h, long long t, unsigned long long& arr_cnt,
                                              unsigned long long& disp_cnt) {
     const int dd = meta & GV_D_MASK;
     const bool ff = meta & GV_FF, exc = meta & GV_EXC;
     const bool arr = (h >> dd) & 1u;
     const bool nxt = (h >> (dd - 1)) & 1u;
     const bool disp = h & 1u;
+    float2 ex = d.gextra[g];  // AMPA (all receptor classes) and the last arrival
+    if (arr) {
+        ex.x = pm_fma(pm_mul(1.0f, st.x), st.y, ex.x);
+        ex.y = pm_ll2f(t);
+    }
+    ex.x = pm_mul(ex.x, k.dec_ampa);
+    d.gextra[g] = ex;
     if (arr && exc) st.z = pm_fma(pm_mul(k.g_nmda, st.x), st.y, st.z);
     st.z = pm_mul(st.z, k.dec_nmda);
     if (ff) st.x = pm_fma(pm_sub(1.0f, st.x), k.rec_ff_step, st.x);
@@ -377,10 +384,37 @@ __device__ __forceinline__ void update_group(const Dev& d, const Consts& k, int 
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(NEU_BLOCK) k_neurons(Dev d, Consts k) {
     __shared__ unsigned s_hist[NEU_BLOCK];
+    __shared__ StepIn s_in;
+    __shared__ float s_gate[NEU_BLOCK];  // gate of column s_colA + q
+    __shared__ int s_colA;
     const Ctrl* c = d.ctrl;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     const int gi = i < d.n_a ? d.a0 + i : d.pf0 + (i - d.n_a);  // global neuron id
-    const long long t = c->t;
+    const int i0 = blockIdx.x * blockDim.x;
+    const int i1 = min(i0 + (int)blockDim.x, d.N);
+    if (threadIdx.x == 0) {
+        s_in = step_inputs(d, k);
+        if (blockIdx.x == 0) publish_step(d, k, s_in);
+    }
+    __syncthreads();
+    const long long t = s_in.t;
+    {   // thalamic gates of the columns whose L4 neurons this CTA holds
+        const int la = min(i1, d.n_a);  // local column neurons are [0, n_a)
+        const int colA = i0 < la ? (d.a0 + i0) / d.NPC : 0;
+        const int colB = i0 < la ? (d.a0 + la - 1) / d.NPC : -1;
+        if (threadIdx.x == 0) s_colA = colA;
+        const int col = colA + (int)threadIdx.x;
+        if (col <= colB) {
+            const int l4_lo = col * d.NPC, l4_hi = l4_lo + d.l4;  // global L4 range
+            const int g_lo = d.a0 + i0, g_hi = d.a0 + la;        // this CTA's column neurons
+            if (l4_lo < g_hi && l4_hi > g_lo) {
+                const float4 g = gate_step(d, col, s_in);
+                s_gate[threadIdx.x] = g.x;
+                if (l4_lo >= g_lo) d.gates[(t & 1) * d.ncol + col] = g;  // holds the column's first neuron
+            }
+        }
+        __syncthreads();
+    }
     const bool valid = i < d.N;
     unsigned spike = 0;
     unsigned hist = 0;
@@ -389,12 +423,12 @@ __global__ void __launch_bounds__(NEU_BLOCK) k_neurons(Dev d, Consts k) {
         const int type = info & 1, region = (info >> 1) & 7, subtype = (info >> 4) & 3;
         const int col = (region != PF) ? (int)(info >> 8) : -1;
         float input = d.input[i];
-        if (c->inject && region == L4) {
+        if (s_in.inject && region == L4) {
             const int off = gi - col * d.NPC;
-            const int b = c->byte;
+            const int b = s_in.byte;
             const int ps = col * k.pref_range;
             const bool in_r = b >= ps && b < ps + k.pref_range;
-            const float v = pm_mul(pm_mul(k.pop_gain, in_r ? k.gain_in : k.gain_out), d.gates[col].x);
+            const float v = pm_mul(pm_mul(k.pop_gain, in_r ? k.gain_in : k.gain_out), s_gate[col - s_colA]);
             unsigned h = (unsigned)b * 2654435761u + (unsigned)col * 0x9E3779B9u;
             for (int q = 0; q < k.pop_k; ++q) {
                 h ^= h << 13; h ^= h >> 17; h ^= h << 5;
@@ -492,9 +526,9 @@ __global__ void __launch_bounds__(NEU_BLOCK) k_neurons(Dev d, Consts k) {
                 atomicAdd(&d.col_sp[(t & 1) * d.ncol + col], 1);
                 if (region == L6) atomicAdd(&d.l6_sp[(t & 1) * d.ncol + col], 1);
             }
-            if (c->inject) {
-                atomicAdd(&d.byte_histogram[c->byte], 1);
-                atomicAdd(&d.neuron_byte_counts[(long long)i * 256 + c->byte], 1);
+            if (s_in.inject) {
+                atomicAdd(&d.byte_histogram[s_in.byte], 1);
+                atomicAdd(&d.neuron_byte_counts[(long long)i * 256 + s_in.byte], 1);
             }
             atomicAdd(&d.ctrl->ltp_visits, (unsigned long long)(d.in_ptr[i + 1] - d.in_ptr[i]));
         }
@@ -508,12 +542,10 @@ __global__ void __launch_bounds__(NEU_BLOCK) k_neurons(Dev d, Consts k) {
     }
     __syncthreads();
     // outgoing synapse groups of this CTA's neurons, one thread per group
-    const int i0 = blockIdx.x * blockDim.x;
-    const int i1 = min(i0 + (int)blockDim.x, d.N);
     const int g0 = d.gbeg[i0], g1 = d.gbeg[i1];
     unsigned long long arr_cnt = 0, disp_cnt = 0;
     auto group_update = [&](int g, unsigned meta, float4 st) {
-        update_group(d, k, g, meta, st, s_hist[gw_lpre(meta)], arr_cnt, disp_cnt);
+        update_group(d, k, g, meta, st, s_hist[gw_lpre(meta)], t, arr_cnt, disp_cnt);
     };
     // two groups per iteration keep independent loads in flight
     const int stride = 2 * blockDim.x;
@@ -568,7 +600,7 @@ __global__ void __launch_bounds__(NEU_BLOCK) k_mirror(Dev d, Consts k) {
         const unsigned h = (d.mhist[m] << 1) | ((d.recv[b >> 5] >> (b & 31)) & 1u);
         d.mhist[m] = h;
         const int ge = d.mbeg[m + 1];
-        for (int g = d.mbeg[m]; g < ge; ++g) update_group(d, k, g, d.gmeta[g], d.gstate[g], h, arr_cnt, disp_cnt);
+        for (int g = d.mbeg[m]; g < ge; ++g) update_group(d, k, g, d.gmeta[g], d.gstate[g], h, t, arr_cnt, disp_cnt);
     }
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) {
@@ -778,7 +810,18 @@ __device__ __forceinline__ void prefetch_l2(const void* ptr) {
 __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d, Consts k) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     __shared__ __align__(8) unsigned long long bars[SYN_WARPS][2];
-    if (blockIdx.x == 0 && threadIdx.x == 0) step_epilogue(d, k);
+    if (blockIdx.x == 0) {
+        if (threadIdx.x == 0) step_epilogue(d, k);
+        // zero the count buffers of step t + 1 (the other parity)
+        const int nb = (int)((d.ctrl->t + 1) & 1);
+        for (int q = d.c0 + threadIdx.x; q < d.c1; q += blockDim.x) {
+            d.col_sp[nb * d.ncol + q] = 0;
+            d.l6_sp[nb * d.ncol + q] = 0;
+        }
+        for (int q = threadIdx.x; q < TD_DIM; q += blockDim.x) d.sub_sp[nb * TD_DIM + q] = 0;
+        if (d.sharded)
+            for (int q = threadIdx.x; q < 1 + TD_DIM; q += blockDim.x) d.send[d.words_max + q] = 0u;
+    }
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const unsigned lt_mask = (1u << lane) - 1u;
     const int cap = d.tile_cap;  // staged elements per stream per buffer
@@ -964,7 +1007,7 @@ struct Engine2e : snnb::Engine {
     snnb::DevBuf<unsigned short> off;
     snnb::DevBuf<unsigned> info, hist, gmeta, gid, byte_hist_nov, raster;
     snnb::DevBuf<float4> gstate, ev, gates;
-    snnb::DevBuf<float2> gview, gcold;
+    snnb::DevBuf<float2> gview, gcold, gextra;
     snnb::DevBuf<float> w_value, w_pred, baseline;
     snnb::DevBuf<Ctrl> ctrl;
     snnb::DevBuf<unsigned char> corpus;
@@ -1011,6 +1054,7 @@ struct Engine2e : snnb::Engine {
         k.off_decay = 0.999f; k.refr_steps = 2;
         k.off_add = (int)pm_mul(0.001f, 256.0f); k.off_max = (int)pm_mul(0.3f, 256.0f);
         k.dec_nmda = snn_expf(pm_div(-1.0f, 150.0f));
+        k.dec_ampa = snn_expf(pm_div(-1.0f, 5.0f));
         k.dec_ca = snn_expf(pm_div(-1.0f, 50.0f));
         k.dec_ca_ff = snn_expf(pm_div(-1.0f, 10.0f));
         k.ca_max = 1.0f; k.ca_max_ff = 0.12f;
@@ -1132,7 +1176,12 @@ struct Engine2e : snnb::Engine {
         D.pw = pw;
         D.words_max = words_max;
         gbeg.upload(h_gbeg.data(), N + 1, stream);
-        gmeta.alloc(G); gsize.alloc(G); gstate.alloc(G); gview.alloc(G); gcold.alloc(G);
+        gmeta.alloc(G); gsize.alloc(G); gstate.alloc(G); gview.alloc(G); gcold.alloc(G); gextra.alloc(G);
+        {
+            std::vector<float2> h_ex(G, make_float2(0.0f, -1000.0f));
+            gextra.upload(h_ex.data(), G, stream);
+            SNN_CUDA(cudaStreamSynchronize(stream));
+        }
         {
             std::vector<unsigned> packed(G);
             std::vector<int> h_gsize(G), h_gpre(G);
@@ -1214,9 +1263,9 @@ struct Engine2e : snnb::Engine {
         h.e0 = cfg.e0;
         h.phase_offset = cfg.phase_offset;
         ctrl.upload(&h, 1, stream);
-        gates.alloc(net.ncol);
-        std::vector<float4> h_g(net.ncol, make_float4(0.5f, 0.0f, 0.0f, 0.0f));
-        gates.upload(h_g.data(), net.ncol, stream);
+        gates.alloc(2 * (size_t)net.ncol);  // state after even / odd steps
+        std::vector<float4> h_g(2 * (size_t)net.ncol, make_float4(0.5f, 0.0f, 0.0f, 0.0f));
+        gates.upload(h_g.data(), 2 * (size_t)net.ncol, stream);
         col_sp.alloc(2 * net.ncol); l6_sp.alloc(2 * net.ncol); sub_sp.alloc(2 * TD_DIM);
         col_sp.zero(stream); l6_sp.zero(stream); sub_sp.zero(stream);
         byte_hist_nov.alloc(256); byte_hist_nov.zero(stream);
@@ -1236,7 +1285,7 @@ struct Engine2e : snnb::Engine {
         D.V = V.p; D.wad = wad.p; D.s = s.p; D.fr = fr.p; D.can = can.p; D.xpost = xpost.p; D.mg = mg.p;
         D.input = input.p; D.nmda_cur = nmda_cur.p; D.last = last.p; D.ref = ref.p; D.off = off.p;
         D.info = info.p; D.hist = hist.p; D.gbeg = gbeg.p; D.in_ptr = in_ptr.p;
-        D.gmeta = gmeta.p; D.gsize = gsize.p; D.gpre = gpre.p; D.gstate = gstate.p; D.gview = gview.p; D.gcold = gcold.p;
+        D.gmeta = gmeta.p; D.gsize = gsize.p; D.gpre = gpre.p; D.gstate = gstate.p; D.gview = gview.p; D.gcold = gcold.p; D.gextra = gextra.p;
         D.tile_cap = tile_cap; D.queue_cap = queue_cap;
         D.gid = gid.p; D.ca = ca.p; D.ev = ev.p; D.act = act.p; D.e1 = e1.p; D.e2 = e2.p; D.val = val.p;
         D.ctrl = ctrl.p; D.gates = gates.p; D.col_sp = col_sp.p; D.l6_sp = l6_sp.p; D.sub_sp = sub_sp.p;
@@ -1274,7 +1323,7 @@ struct Engine2e : snnb::Engine {
 
     // kernels (timing slots) per step: control, neurons, [exchange + mirror
     // groups when sharded], synapses
-    int nslot() const { return world > 1 ? 4 : 3; }
+    int nslot() const { return world > 1 ? 3 : 2; }
 
     // one step; with profiling, events ev[0..nslot] bracket the slots
     // (inside a stream capture the records must be "external" so that they
@@ -1283,8 +1332,6 @@ struct Engine2e : snnb::Engine {
         const int nb = (D.N + NEU_BLOCK - 1) / NEU_BLOCK;
         const unsigned fl = capturing ? cudaEventRecordExternal : cudaEventRecordDefault;
         int e = 0;
-        if (ev) SNN_CUDA(cudaEventRecordWithFlags(ev[e++], st, fl));
-        k_control<<<1, CTL_THREADS, 0, st>>>(D, K);
         if (ev) SNN_CUDA(cudaEventRecordWithFlags(ev[e++], st, fl));
         k_neurons<<<nb, NEU_BLOCK, 0, st>>>(D, K);
         if (ev) SNN_CUDA(cudaEventRecordWithFlags(ev[e++], st, fl));
@@ -1349,7 +1396,6 @@ struct Engine2e : snnb::Engine {
         drop_graph();
         memset(&prof, 0, sizeof(prof));
         int q = 0;
-        strcpy(prof.names[q++], "k_control");
         strcpy(prof.names[q++], "k_neurons");
         if (world > 1) strcpy(prof.names[q++], "allgather+k_mirror");
         strcpy(prof.names[q++], "k_synapses");
@@ -1486,6 +1532,26 @@ struct Engine2e : snnb::Engine {
         SNN_CUDA(cudaStreamSynchronize(stream));
     }
 
+    // device group of every kept synapse, in the reference (pre-major) order
+    std::vector<uint32_t> sid_group_cache;
+    const std::vector<uint32_t>& sid_groups() {
+        if (!sid_group_cache.empty() || net.S == 0) return sid_group_cache;
+        sid_group_cache.resize(net.S);
+        for (int pre = 0; pre < net.N; ++pre) {
+            for (int32_t sid = net.row_ptr[pre]; sid < net.row_ptr[pre + 1]; ++sid) {
+                const int key = eff_delay(net.delay[sid]) * 2 + ((net.flags[sid] & RF_FF) ? 1 : 0);
+                int g = lay.gbeg[pre];
+                while (g < lay.gbeg[pre + 1]) {
+                    const uint32_t m = lay.gmeta[g];
+                    if ((int)((m & GV_D_MASK) * 2 + ((m & GV_FF) ? 1 : 0)) == key) break;
+                    ++g;
+                }
+                sid_group_cache[sid] = (uint32_t)new_of_old[g];
+            }
+        }
+        return sid_group_cache;
+    }
+
     template <typename T>
     std::vector<T> fetch(const snnb::DevBuf<T>& b, size_t n) {
         std::vector<T> h(n);
@@ -1519,25 +1585,23 @@ struct Engine2e : snnb::Engine {
             for (int64_t p = 0; p < S; ++p) o[lay.perm[p]] = pm[p];
         };
         // group state -> per synapse (pre-major)
+        (void)NG;
         auto syn_group = [&](int comp) {
             need(S * 4);
             auto gs = fetch(gstate, lay.G);
+            const auto& sg = sid_groups();
             float* o = (float*)buf;
-            for (int pre = 0; pre < NG; ++pre) {
-                for (int32_t sid = net.row_ptr[pre]; sid < net.row_ptr[pre + 1]; ++sid) {
-                    int key = eff_delay(net.delay[sid]) * 2 + ((net.flags[sid] & RF_FF) ? 1 : 0);
-                    int g = lay.gbeg[pre];
-                    while (g < lay.gbeg[pre + 1]) {
-                        uint32_t m = lay.gmeta[g];
-                        if ((int)((m & GV_D_MASK) * 2 + ((m & GV_FF) ? 1 : 0)) == key) break;
-                        ++g;
-                    }
-                    const float4 v = gs[new_of_old[g]];
-                    float x = comp == 0 ? v.x : comp == 1 ? v.y : comp == 2 ? v.z : v.w;
-                    // inhibitory synapses never gain NMDA conductance
-                    o[sid] = x;
-                }
+            for (int64_t sid = 0; sid < S; ++sid) {
+                const float4 v = gs[sg[sid]];
+                o[sid] = comp == 0 ? v.x : comp == 1 ? v.y : comp == 2 ? v.z : v.w;
             }
+        };
+        auto syn_extra = [&](int comp) {
+            need(S * 4);
+            auto gx = fetch(gextra, lay.G);
+            const auto& sg = sid_groups();
+            float* o = (float*)buf;
+            for (int64_t sid = 0; sid < S; ++sid) o[sid] = comp == 0 ? gx[sg[sid]].x : gx[sg[sid]].y;
         };
         auto ev_comp = [&](int comp) {
             auto h = fetch(ev, S);
@@ -1587,13 +1651,17 @@ struct Engine2e : snnb::Engine {
             case SNN_STATE_UTIL: syn_group(1); break;
             case SNN_STATE_NMDA_G: syn_group(2); break;
             case SNN_STATE_X_PRE: syn_group(3); break;
+            case SNN_STATE_AMPA: syn_extra(0); break;
+            case SNN_STATE_LAST_PRE: syn_extra(1); break;
             case SNN_STATE_POST: need(S * 4); memcpy(buf, net.post.data(), S * 4); break;
             case SNN_STATE_DELAY: need(S); memcpy(buf, net.delay.data(), S); break;
             case SNN_STATE_FLAGS: need(S); memcpy(buf, net.flags.data(), S); break;
             case SNN_STATE_ROW_PTR: need((int64_t)(NG + 1) * 4); memcpy(buf, net.row_ptr.data(), (NG + 1) * 4); break;
             case SNN_STATE_GATES: {
                 need((int64_t)net.ncol * 16);
-                gates.download((float4*)buf, net.ncol, stream);
+                const size_t half = steps > 0 ? (size_t)((steps - 1) & 1) : 1;  // after the last step
+                SNN_CUDA(cudaMemcpyAsync(buf, gates.p + half * net.ncol, (size_t)net.ncol * sizeof(float4),
+                                         cudaMemcpyDeviceToHost, stream));
                 SNN_CUDA(cudaStreamSynchronize(stream));
                 break;
             }
@@ -1628,11 +1696,130 @@ struct Engine2e : snnb::Engine {
         SNN_CUDA(cudaStreamSynchronize(stream));
     }
 
-    void save(const char*, int32_t) override {
-        throw snnb::Error(SNN_ERR_UNSUPPORTED, "stage2e save not implemented yet");
+    // ---- checkpoints ------------------------------------------------------
+    struct NativeBlob {  // host-side state + a fingerprint of the network
+        int64_t steps, raster_base, N, S, G, M;
+        int32_t rank, world, ncol, raster_cap;
+    };
+    std::vector<snnb::DevSection> native_sections() {
+        std::vector<snnb::DevSection> v;
+        auto add = [&](const char* n, auto& b) { v.push_back({n, (void*)b.p, b.bytes()}); };
+        add("V", V); add("wad", wad); add("s", s); add("fr", fr); add("can", can);
+        add("xpost", xpost); add("mg", mg); add("input", input); add("nmda_cur", nmda_cur);
+        add("last", last); add("ref", ref); add("off", off); add("hist", hist);
+        add("gstate", gstate); add("gview", gview); add("gcold", gcold); add("gextra", gextra);
+        add("ca", ca); add("ev", ev); add("act", act); add("e1", e1); add("e2", e2); add("val", val);
+        add("ctrl", ctrl); add("gates", gates); add("col_sp", col_sp); add("l6_sp", l6_sp);
+        add("sub_sp", sub_sp); add("byte_hist_nov", byte_hist_nov); add("byte_histogram", byte_histogram);
+        add("neuron_byte_counts", neuron_byte_counts); add("w_value", w_value); add("w_pred", w_pred);
+        add("baseline", baseline); add("raster", raster); add("mhist", mhist);
+        return v;
     }
-    void load(const char*, int32_t) override {
-        throw snnb::Error(SNN_ERR_UNSUPPORTED, "stage2e load not implemented yet");
+    NativeBlob blob() const {
+        NativeBlob b{};
+        b.steps = steps; b.raster_base = raster_base_host; b.N = D.N; b.S = net.S; b.G = lay.G; b.M = D.M;
+        b.rank = rank; b.world = world; b.ncol = net.ncol; b.raster_cap = raster_cap;
+        return b;
+    }
+
+    // SCKP v2 (src/stage2e/scheduler.cu:411-483): this rank's synapses as the
+    // reference's 80-byte BioSynapse records in reference synapse order, the
+    // neuron x byte counts, alpha, beta; `step` = steps executed
+    struct BioSyn {
+        int32_t pre, post;
+        float weight, delay_steps, last_pre, last_post, x_pre, x_post;
+        float nmda, ampa, ca, resource, elig, elig_slow, util, scaling;
+        float autoph, da_r, ach_r;
+        uint8_t flags, ne_u8, ht5_u8, pad;
+    };
+    static_assert(sizeof(BioSyn) == 80, "BioSynapse record");
+    void write_sckp(const char* path) {
+        const int64_t S = net.S;
+        SNN_REQUIRE(S < (1ll << 32) && D.N >= 0, SNN_ERR_ARG, "too many synapses for SCKP v2");
+        auto gs = fetch(gstate, lay.G);
+        auto gx = fetch(gextra, lay.G);
+        auto evh = fetch(ev, S);
+        auto cah = fetch(ca, S);
+        auto xp = fetch(xpost, D.N);
+        auto lst = fetch(last, D.N);
+        const auto& sg = sid_groups();
+        std::vector<BioSyn> aos(S);
+        std::vector<float> al(S), be(S);
+        const uint8_t r38 = (uint8_t)pm_mul(0.3f, 127.0f);
+        for (int pre = 0; pre < net.N; ++pre) {
+            for (int32_t sid = net.row_ptr[pre]; sid < net.row_ptr[pre + 1]; ++sid) {
+                BioSyn& b = aos[sid];
+                memset(&b, 0, sizeof(b));
+                const int post = net.post[sid];
+                const int lp = sh.local_of(post);
+                const bool exc = net.flags[sid] & (RF_AMPA | RF_NMDA);
+                const float4 g = gs[sg[sid]];
+                const float2 x = gx[sg[sid]];
+                b.pre = pre; b.post = post;
+                b.delay_steps = pm_i2f(net.delay[sid]);
+                b.last_pre = x.y; b.last_post = pm_i2f(lst[lp]);
+                b.x_pre = g.w; b.x_post = xp[lp];
+                b.nmda = g.z; b.ampa = x.x; b.resource = g.x; b.util = g.y;
+                b.elig_slow = 0.0f; b.scaling = 1.0f;
+                b.da_r = exc ? 0.5f : -0.3f; b.ach_r = 0.3f;
+                b.flags = net.flags[sid]; b.ne_u8 = r38; b.ht5_u8 = r38;
+            }
+        }
+        for (int64_t p = 0; p < S; ++p) {
+            const int32_t sid = lay.perm[p];
+            BioSyn& b = aos[sid];
+            const float4 e = evh[p];
+            const float m = pm_div(pm_mul(1.5f, e.x), pm_add(e.x, e.y));
+            b.weight = (b.flags & (RF_AMPA | RF_NMDA)) ? m : -m;
+            b.ca = cah[p]; b.elig = e.w; b.autoph = e.z;
+            al[sid] = e.x; be[sid] = e.y;
+        }
+        auto nbc = fetch(neuron_byte_counts, (size_t)D.N * 256);
+        snnb::BinFile f(path, true);
+        const uint32_t hdr[5] = {0x53434B50u, 2u, (uint32_t)steps, (uint32_t)S, (uint32_t)D.N};
+        f.put(hdr, sizeof(hdr));
+        f.put(aos.data(), sizeof(BioSyn) * (size_t)S);
+        f.put(nbc.data(), sizeof(int) * nbc.size());
+        f.put(al.data(), 4 * (size_t)S);
+        f.put(be.data(), 4 * (size_t)S);
+        f.close();
+    }
+
+    void save(const char* path, int32_t fmt) override {
+        SNN_REQUIRE(built, SNN_ERR_STATE, "build the network first");
+        SNN_CUDA(cudaStreamSynchronize(stream));
+        if (fmt == SNN_FMT_NATIVE) {
+            const NativeBlob b = blob();
+            snnb::save_native(path, SNN_MODEL_STAGE2E, &b, sizeof(b), native_sections(), stream);
+        } else if (fmt == SNN_FMT_SCKP_V2) {
+            write_sckp(path);
+        } else if (fmt == SNN_FMT_RAW_F32) {  // weights in reference synapse order
+            std::vector<float> w(net.S);
+            get_state(SNN_STATE_WEIGHT, w.data(), (int64_t)w.size() * 4);
+            snnb::BinFile f(path, true);
+            f.put(w.data(), w.size() * 4);
+            f.close();
+        } else {
+            throw snnb::Error(SNN_ERR_UNSUPPORTED, "Stage 2e writes the native, SCKP v2 and raw formats");
+        }
+    }
+    void load(const char* path, int32_t fmt) override {
+        SNN_REQUIRE(built, SNN_ERR_STATE, "build the network first");
+        SNN_REQUIRE(fmt == SNN_FMT_NATIVE, SNN_ERR_UNSUPPORTED,
+                    "Stage 2e resumes from the native format (SCKP v2 has no reader in the reference)");
+        const NativeBlob want = blob();
+        NativeBlob got{};
+        snnb::load_native(path, SNN_MODEL_STAGE2E, &got, sizeof(got), native_sections(), stream,
+                          [&](const void* p) {
+                              NativeBlob f;
+                              memcpy(&f, p, sizeof(f));
+                              SNN_REQUIRE(f.N == want.N && f.S == want.S && f.G == want.G && f.M == want.M &&
+                                              f.rank == want.rank && f.world == want.world &&
+                                              f.ncol == want.ncol && f.raster_cap == want.raster_cap,
+                                          SNN_ERR_IO, "checkpoint of another network or shard");
+                          });
+        steps = got.steps;
+        raster_base_host = got.raster_base;
     }
 };
 

@@ -19,6 +19,7 @@
 // graph), advanced by a one-thread kernel at the end of each launch.
 #include <algorithm>
 #include <mutex>
+#include "ckpt.h"
 #include "common.h"
 #include "snn_prop_rules.h"
 
@@ -1037,11 +1038,53 @@ struct EngineProp : snnb::Engine {
         SNN_CUDA(cudaStreamSynchronize(stream));
     }
 
-    void save(const char*, int32_t) override {
-        throw snnb::Error(SNN_ERR_UNSUPPORTED, "the propagation microbench has no checkpoint format");
+    // native full state (SNN_FMT_NATIVE) for bit-exact resume
+    struct NativeBlob {
+        int64_t steps, raster_base, N, S;
+        float dopamine, w_max;
+        int32_t mode, raster_cap;
+        uint32_t thr, pad;
+    };
+    NativeBlob blob() const {
+        NativeBlob b{};
+        b.steps = steps; b.raster_base = raster_base_host; b.N = D.N; b.S = S;
+        b.dopamine = dopamine; b.w_max = D.w_max; b.mode = mode; b.raster_cap = raster_cap; b.thr = D.thr;
+        return b;
     }
-    void load(const char*, int32_t) override {
-        throw snnb::Error(SNN_ERR_UNSUPPORTED, "the propagation microbench has no checkpoint format");
+    std::vector<snnb::DevSection> native_sections() {
+        std::vector<snnb::DevSection> v;
+        auto add = [&](const char* n, auto& b) {
+            if (b.p) v.push_back({n, (void*)b.p, b.bytes()});
+        };
+        add("acc", acc); add("V", V); add("I", I); add("ref", ref); add("last_post", last_post);
+        add("w", w); add("tA", tA); add("tB", tB); add("u", u); add("R", R); add("pre_list", pre_list);
+        add("rel_list", rel_list); add("un_list", un_list); add("rn_list", rn_list);
+        add("post_list", post_list); add("raster", raster); add("ctrl", ctrl);
+        return v;
+    }
+    void save(const char* path, int32_t fmt) override {
+        SNN_REQUIRE(built, SNN_ERR_STATE, "build the network first");
+        SNN_REQUIRE(fmt == SNN_FMT_NATIVE, SNN_ERR_UNSUPPORTED, "the microbench writes the native format only");
+        const NativeBlob b = blob();
+        snnb::save_native(path, SNN_MODEL_PROP, &b, sizeof(b), native_sections(), stream);
+    }
+    void load(const char* path, int32_t fmt) override {
+        SNN_REQUIRE(built, SNN_ERR_STATE, "build the network first");
+        SNN_REQUIRE(fmt == SNN_FMT_NATIVE, SNN_ERR_UNSUPPORTED, "the microbench reads the native format only");
+        const NativeBlob want = blob();
+        NativeBlob got{};
+        snnb::load_native(path, SNN_MODEL_PROP, &got, sizeof(got), native_sections(), stream,
+                          [&](const void* p) {
+                              NativeBlob f;
+                              memcpy(&f, p, sizeof(f));
+                              SNN_REQUIRE(f.N == want.N && f.S == want.S && f.mode == want.mode &&
+                                              f.thr == want.thr && f.raster_cap == want.raster_cap &&
+                                              f.w_max == want.w_max,
+                                          SNN_ERR_IO, "checkpoint of another microbench network");
+                          });
+        steps = got.steps;
+        raster_base_host = got.raster_base;
+        dopamine = got.dopamine;
     }
 };
 

@@ -39,6 +39,7 @@ STATE = {
     "R": (26, np.float32, "S"), "u": (27, np.float32, "S"), "elig": (28, np.float32, "S"),
     "camkii_act": (29, np.float32, "S"), "autophos": (30, np.float32, "S"),
     "e1": (31, np.float32, "S"), "e2": (32, np.float32, "S"),
+    "ampa": (33, np.float32, "S"), "last_pre": (34, np.float32, "S"),
     "post": (40, np.int32, "S"), "delay": (41, np.uint8, "S"), "row_ptr": (42, np.int32, "N1"),
     "flags": (43, np.uint8, "S"), "gates": (50, np.float32, "G4"),
     "modulators": (51, np.float32, "4"), "byte_hist": (52, np.int32, "256"),

@@ -15,7 +15,7 @@ import pyoracle as po
 import snn_b200 as snn
 
 SYN_FIELDS = ["alpha", "beta", "weight", "x_pre", "nmda", "ca", "R", "u", "elig",
-              "camkii_act", "autophos", "e1", "e2"]
+              "camkii_act", "autophos", "e1", "e2", "ampa", "last_pre"]
 NEU_FIELDS = [("V", "V"), ("w", "w"), ("s", "s"), ("fr", "fr"), ("ca_neuron", "ca"),
               ("nmda_cur", "nmda_cur")]
 
