@@ -107,14 +107,14 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def profile_traffic(name):
-    """DRAM bytes per launch (read + write) recorded from an ncu capture in
-    profiles/<name> as `traffic_bytes_per_launch = N`, or None."""
+def profile_traffic(name, key="traffic_bytes_per_launch"):
+    """A DRAM traffic figure (read + write) recorded from an ncu capture in
+    profiles/<name> as `<key> = N`, or None."""
     import re
     p = os.path.join(ROOT, "profiles", name)
     if not os.path.exists(p):
         return None
-    m = re.search(r"traffic_bytes_per_launch\s*=\s*([0-9.eE+]+)", open(p).read())
+    m = re.search(key + r"\s*=\s*([0-9.eE+]+)", open(p).read())
     return float(m.group(1)) if m else None
 
 
@@ -212,6 +212,8 @@ def prop_main(args):
     rates = [float(x) for x in args.prop_rates.split(",")] if args.prop_rates else PROP_RATES
     modes = [m for m in PROP_MODES if not args.prop_modes or str(m[0]) in args.prop_modes.split(",")]
     n_neu = args.prop_neurons
+    # ncu: DRAM bytes per event of the bucketed push (plain propagation)
+    traffic_per_event = profile_traffic("k4_push_b_propagation_1M.md", "traffic_bytes_per_event")
     for mode, mname in modes:
         for rate in rates:
             net = snn.Network(model=snn.MODEL_PROP, prop_mode=mode, prop_rate=rate)
@@ -265,7 +267,9 @@ def prop_main(args):
                                         for k, v in prof["kernels"].items()},
                 "roofline": {"bound": "hbm", "kernel": pname, "achieved": achieved,
                              "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                             "peak_kind": peak_kind, "bytes_per_launch": pb, "traffic": None},
+                             "peak_kind": peak_kind, "bytes_per_launch": pb,
+                             "traffic": traffic_per_event * ev / args.steps
+                             if pname == "k4_push_b" and mode == 0 and traffic_per_event else None},
                 "clocks": clk.summary(),
             }
             if cb:
