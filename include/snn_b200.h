@@ -225,9 +225,12 @@ int snn_get_state(snn_ctx* ctx, int32_t which, void* host_buf, int64_t n_bytes);
 int snn_get_counters(snn_ctx* ctx, snn_counters* out);
 int snn_set_dopamine(snn_ctx* ctx, float level);
 int snn_set_e0(snn_ctx* ctx, int32_t enable);
-/* Device timing of the engine's kernels: CUDA events recorded on the engine
- * stream around every kernel of every step (captured into the step graph).
- * Cumulative since snn_set_profiling(ctx, 1). */
+/* Device timing of the engine's kernels: with level 1, CUDA events recorded
+ * on the engine stream around every kernel of every step (captured into the
+ * step graph), cumulative since snn_set_profiling(ctx, 1).  With level 2
+ * (Stage 2e engine) only one event pair around each snn_run / snn_step call:
+ * step_ms and steps without per-kernel slots and without events inside the
+ * steps; other engines treat 2 as 1. */
 typedef struct snn_profile {
     int64_t steps;           /* steps timed                                  */
     int32_t n_kernels;       /* kernels per step                              */

@@ -996,8 +996,11 @@ struct Engine2e : snnb::Engine {
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t graph_exec = nullptr;
     int graph_steps = 0;
-    // profiling: events around every kernel (3 kernels per step)
+    // profiling: level 1 = events around every kernel of every step; level 2
+    // = one event pair around each run call (no event inside the steps)
     bool profiling = false;
+    int prof_level = 0;
+    cudaEvent_t run_ev[2] = {nullptr, nullptr};
     std::vector<cudaEvent_t> pev;
     snn_profile prof{};
     // device buffers
@@ -1032,6 +1035,8 @@ struct Engine2e : snnb::Engine {
     }
     ~Engine2e() override {
         for (auto e : pev) cudaEventDestroy(e);
+        for (auto e : run_ev)
+            if (e) cudaEventDestroy(e);
         // graphs holding NCCL calls go before the communicator
         if (graph_exec) cudaGraphExecDestroy(graph_exec);
         if (graph) cudaGraphDestroy(graph);
@@ -1391,8 +1396,14 @@ struct Engine2e : snnb::Engine {
 
     void set_profiling(int32_t en) override {
         SNN_REQUIRE(built, SNN_ERR_STATE, "build the network first");
+        SNN_REQUIRE(en >= 0 && en <= 2, SNN_ERR_ARG, "profiling level must be 0, 1 or 2");
         SNN_CUDA(cudaStreamSynchronize(stream));
-        profiling = en != 0;
+        prof_level = en;
+        profiling = en == 1;
+        if (en == 2 && !run_ev[0]) {
+            SNN_CUDA(cudaEventCreate(&run_ev[0]));
+            SNN_CUDA(cudaEventCreate(&run_ev[1]));
+        }
         drop_graph();
         memset(&prof, 0, sizeof(prof));
         int q = 0;
@@ -1425,6 +1436,10 @@ struct Engine2e : snnb::Engine {
         }
         int done = 0;
         const int chunk = 50;
+        if (prof_level == 2) {  // graph built before the first event: no host work timed
+            if (n_steps >= chunk) ensure_graph(chunk);
+            SNN_CUDA(cudaEventRecord(run_ev[0], stream));
+        }
         while (done < n_steps) {
             int left = n_steps - done;
             // raster rows wrap every raster_cap steps: drain before overwriting
@@ -1466,6 +1481,14 @@ struct Engine2e : snnb::Engine {
                 SNN_CUDA(cudaStreamSynchronize(stream));
             }
             done += span;
+        }
+        if (prof_level == 2) {
+            SNN_CUDA(cudaEventRecord(run_ev[1], stream));
+            SNN_CUDA(cudaEventSynchronize(run_ev[1]));
+            float ms = 0.0f;
+            SNN_CUDA(cudaEventElapsedTime(&ms, run_ev[0], run_ev[1]));
+            prof.step_ms += ms;
+            prof.steps += n_steps;
         }
         steps += n_steps;
         SNN_CUDA(cudaGetLastError());

@@ -308,6 +308,8 @@ class Network:
         return c.as_dict()
 
     def set_profiling(self, enable=True):
+        """True / 1: per-kernel device times; 2: whole-run device time only
+        (Stage 2e); False / 0: off."""
         self._check(self.L.snn_set_profiling(self.h, int(enable)))
 
     def profile(self):
