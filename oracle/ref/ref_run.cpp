@@ -7,6 +7,11 @@
 //       after every step: "step count fnv64(spiking indices)" to OUT.txt; at
 //       the end, V / w / fire-rate of every neuron and the summed alpha/beta
 //       to OUT.bin.  Used to pin the CPU oracle against the reference itself.
+//   ref_run --steps K [--corpus F] --stats OUT.bin
+//       K steps, then i32 N, i32 S, i32 K, per-neuron spike counts over the
+//       run (i32[N]), fire rates (f32[N]), alpha (f32[S]), beta (f32[S]),
+//       receptor flags (u8[S]) and the neuron x byte counts (i32[N*256]):
+//       the long-run statistics the tests compare with this library's engine.
 //   ref_run --steps K [--corpus F] --time W
 //       W untimed warm-up steps, then K timed steps of the reference's own
 //       host loop (src/stage2e/main.cpp:679-743, without CSV); prints
@@ -36,11 +41,13 @@ int main(int argc, char** argv) {
     const char* corpus = nullptr;
     const char* dump = nullptr;
     const char* state = nullptr;
+    const char* stats = nullptr;
     for (int i = 1; i < argc; ++i) {
         if (!strcmp(argv[i], "--steps") && i + 1 < argc) steps = atoi(argv[++i]);
         else if (!strcmp(argv[i], "--corpus") && i + 1 < argc) corpus = argv[++i];
         else if (!strcmp(argv[i], "--dump") && i + 1 < argc) dump = argv[++i];
         else if (!strcmp(argv[i], "--state") && i + 1 < argc) state = argv[++i];
+        else if (!strcmp(argv[i], "--stats") && i + 1 < argc) stats = argv[++i];
         else if (!strcmp(argv[i], "--time") && i + 1 < argc) warm = atoi(argv[++i]);
     }
     int dev_count = 0;
@@ -77,8 +84,13 @@ int main(int argc, char** argv) {
     FILE* f = dump ? fopen(dump, "w") : nullptr;
     std::vector<uint8_t> flags(N);
     std::vector<int32_t> idx;
+    std::vector<int32_t> counts(stats ? N : 0, 0);
     for (int s = 0; s < steps; ++s) {
         sched.step(s);
+        if (stats) {
+            cudaMemcpy(flags.data(), alloc.buffers().d_spike_flags, N, cudaMemcpyDeviceToHost);
+            for (int i = 0; i < N; ++i) counts[i] += flags[i] ? 1 : 0;
+        }
         if (f) {
             cudaMemcpy(flags.data(), alloc.buffers().d_spike_flags, N, cudaMemcpyDeviceToHost);
             idx.clear();
@@ -110,6 +122,32 @@ int main(int argc, char** argv) {
             fwrite(&sb, 8, 1, g);
             fclose(g);
         }
+    }
+    if (stats) {
+        const int S = N_TOTAL_SYNAPSES_2E;
+        std::vector<NeuronStateAdEx> h(N);
+        cudaMemcpy(h.data(), alloc.buffers().d_neurons, N * sizeof(NeuronStateAdEx), cudaMemcpyDeviceToHost);
+        std::vector<float> fr(N), a(S), b(S);
+        for (int i = 0; i < N; ++i) fr[i] = h[i].fire_rate;
+        cudaMemcpy(a.data(), alloc.buffers().d_synapse_alpha, (size_t)S * 4, cudaMemcpyDeviceToHost);
+        cudaMemcpy(b.data(), alloc.buffers().d_synapse_beta, (size_t)S * 4, cudaMemcpyDeviceToHost);
+        std::vector<BioSynapse> syn(S);
+        cudaMemcpy(syn.data(), alloc.buffers().d_synapses, (size_t)S * sizeof(BioSynapse), cudaMemcpyDeviceToHost);
+        std::vector<uint8_t> rf(S);
+        for (int q = 0; q < S; ++q) rf[q] = syn[q].receptor_flags;
+        std::vector<int32_t> nbc((size_t)N * 256);
+        cudaMemcpy(nbc.data(), alloc.buffers().d_neuron_byte_counts, nbc.size() * 4, cudaMemcpyDeviceToHost);
+        FILE* g = fopen(stats, "wb");
+        if (!g) { fprintf(stderr, "ref_run: cannot write %s\n", stats); return 7; }
+        const int32_t hdr[3] = {N, S, steps};
+        fwrite(hdr, 4, 3, g);
+        fwrite(counts.data(), 4, N, g);
+        fwrite(fr.data(), 4, N, g);
+        fwrite(a.data(), 4, S, g);
+        fwrite(b.data(), 4, S, g);
+        fwrite(rf.data(), 1, S, g);
+        fwrite(nbc.data(), 4, nbc.size(), g);
+        fclose(g);
     }
     cudaError_t e = cudaDeviceSynchronize();
     if (e != cudaSuccess) { fprintf(stderr, "ref_run: %s\n", cudaGetErrorString(e)); return 6; }
