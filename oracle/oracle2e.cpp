@@ -86,6 +86,7 @@ struct O2eParams {
     int32_t e0;               // E0 ablation
     int32_t phase_offset;     // added to the step for the phase-table lookup
     int32_t n_threads;        // OpenMP threads (0 = library default)
+    int32_t preset;           // 0 reference constants, 1 the benchmark's AdEx / STP constants
 };
 
 struct Syn {  // mirrors the 80-byte BioSynapse (src/stage2e/types.h:66-101)
@@ -185,6 +186,8 @@ struct Oracle {
     // constants (host computed exactly as the reference's constant folds)
     float dec_nmda, dec_ampa, dec_ca, dec_ca_ff, rec_ff_step, dec_xpre, dec_xpost;
     float fac_ff, rec_ff, fac_exc, rec_exc, fac_inh, rec_inh;
+    float U_ff, U_exc, U_inh;              // STP utilisation by class
+    float vt, dT, a_ad, b_ad;              // AdEx in the reference's normalised units
     float e1_dec, e2_dec, ca_n_dec, inv_taum, inv_tauw;
     float mod_dec[4];
     float ne_r, ht5_r;
@@ -456,6 +459,22 @@ void setup(Oracle& o) {
     o.ca_n_dec = pm_sub(1.0f, pm_div(1.0f, 50.0f));
     o.inv_taum = pm_div(1.0f, 9.37f);
     o.inv_tauw = pm_div(1.0f, 144.0f);
+    o.U_ff = 0.02f; o.U_exc = 0.2f; o.U_inh = 0.05f;
+    o.vt = 0.8f; o.dT = 0.1f; o.a_ad = 0.0133f; o.b_ad = 0.0805f;
+    if (o.P.preset == 1) {
+        // benchmark constants (C 200 pF, gL 10 nS, EL -70 mV, VT -50 mV, dT 2 mV,
+        // a 2 nS, b 0.08 nA, tau_w 100 ms, dt 1 ms) in the reference's units:
+        // v = (V - EL) / 25 mV (VT -> 0.8, spike at 1), w in gL * 25 mV;
+        // STP U 0.5, tau_d 200, tau_f 50 for every class (FF per-step recovery too)
+        o.inv_taum = pm_div(1.0f, 20.0f);
+        o.inv_tauw = pm_div(1.0f, 100.0f);
+        o.vt = 0.8f; o.dT = 0.08f; o.a_ad = 0.2f; o.b_ad = 0.32f;
+        o.U_ff = o.U_exc = o.U_inh = 0.5f;
+        o.fac_ff = o.fac_exc = o.fac_inh = snn_expf(pm_div(-1.0f, 50.0f));
+        o.rec_ff = o.rec_exc = o.rec_inh = pm_sub(1.0f, snn_expf(pm_div(-1.0f, 200.0f)));
+        o.rec_ff_step = o.rec_ff;
+        for (auto& sy : o.syn) sy.u = 0.5f;
+    }
     o.mod_dec[0] = snn_expf(pm_div(-100.0f, 100.0f));
     o.mod_dec[1] = snn_expf(pm_div(-100.0f, 200.0f));
     o.mod_dec[2] = snn_expf(pm_div(-100.0f, 150.0f));
@@ -592,12 +611,12 @@ void step(Oracle& o) {
         n.s = pm_fma(n.s, 0.7f, pm_mul(o.input[i], 0.3f));
         float I = pm_sub(pm_add(n.s, o.nmda_cur[i]), o.inh[i]);
         float V = n.V, w = n.w;
-        float ea = pm_div(pm_sub(V, 0.8f), 0.1f);
+        float ea = pm_div(pm_sub(V, o.vt), o.dT);
         if (ea > 10.0f) ea = 10.0f;
         if (ea < -10.0f) ea = -10.0f;
-        float et = pm_mul(0.1f, snn_expf(ea));
+        float et = pm_mul(o.dT, snn_expf(ea));
         float dV = pm_mul(pm_add(pm_sub(pm_add(-V, et), w), I), o.inv_taum);
-        float dw = pm_mul(pm_fma(0.0133f, V, -w), o.inv_tauw);
+        float dw = pm_mul(pm_fma(o.a_ad, V, -w), o.inv_tauw);
         V = pm_add(V, dV);
         w = pm_add(w, dw);
         if (V < -0.5f) V = -0.5f;
@@ -610,7 +629,7 @@ void step(Oracle& o) {
             n.last = (int32_t)t;
             n.ref = 2;
             V = 0.0f;
-            w = pm_add(w, 0.0805f);
+            w = pm_add(w, o.b_ad);
             n.ca = fminf(pm_add(n.ca, 0.2f), 1.0f);
             n.fr = pm_fma(n.fr, 0.9f, 0.1f);
             int no = (int)n.off + (int)pm_mul(0.001f, 256.0f);
@@ -732,9 +751,9 @@ void step(Oracle& o) {
     for (auto& ar : arrived) {
         Syn& s = o.syn[ar.first];
         float U, fac, rec;
-        if (s.flags & FLAG_FF) { U = 0.02f; fac = o.fac_ff; rec = o.rec_ff; }
-        else if (s.flags & 0x03) { U = 0.2f; fac = o.fac_exc; rec = o.rec_exc; }
-        else { U = 0.05f; fac = o.fac_inh; rec = o.rec_inh; }
+        if (s.flags & FLAG_FF) { U = o.U_ff; fac = o.fac_ff; rec = o.rec_ff; }
+        else if (s.flags & 0x03) { U = o.U_exc; fac = o.fac_exc; rec = o.rec_exc; }
+        else { U = o.U_inh; fac = o.fac_inh; rec = o.rec_inh; }
         s.R = pm_fma(pm_sub(1.0f, s.R), rec, s.R);
         s.u = pm_fma(pm_sub(s.u, U), fac, U);
         float un = pm_fma(U, pm_sub(1.0f, s.u), s.u);

@@ -21,7 +21,7 @@ class O2eParams(C.Structure):
         ("deg_inter", C.c_int32), ("deg_l5_pf", C.c_int32),
         ("deg_pf_self", C.c_int32), ("deg_pf_assoc", C.c_int32),
         ("total_synapses", C.c_int64), ("seed", C.c_uint32), ("e0", C.c_int32),
-        ("phase_offset", C.c_int32), ("n_threads", C.c_int32),
+        ("phase_offset", C.c_int32), ("n_threads", C.c_int32), ("preset", C.c_int32),
     ]
 
 
@@ -78,9 +78,10 @@ def lib():
     return _lib
 
 
-def ref_params(n_columns=50, seed=42, e0=0, phase_offset=0, n_threads=0):
+def ref_params(n_columns=50, seed=42, e0=0, phase_offset=0, n_threads=0, preset=0):
     """Reference topology rules (src/stage2e/network_init.cu:198-233), scaled by
-    column count; n_columns=50 is the reference network (55,000 / 10,700,000)."""
+    column count; n_columns=50 is the reference network (55,000 / 10,700,000).
+    preset 0: the reference's constants; 1: the benchmark's AdEx / STP ones."""
     p = O2eParams()
     p.n_columns = n_columns
     p.l4, p.l23, p.l5, p.l6 = 200, 350, 200, 250
@@ -89,6 +90,7 @@ def ref_params(n_columns=50, seed=42, e0=0, phase_offset=0, n_threads=0):
     p.deg_pf_self, p.deg_pf_assoc = 100, 50
     p.total_synapses = 10_700_000 * n_columns // 50
     p.seed, p.e0, p.phase_offset, p.n_threads = seed, e0, phase_offset, n_threads
+    p.preset = preset
     return p
 
 

@@ -1088,6 +1088,22 @@ struct Engine2e : snnb::Engine {
         k.rec_ne = pm_div(pm_u2f((unsigned)pm_mul(0.3f, 127.0f)), 127.0f);
         k.rec_ht5 = k.rec_ne;
         k.pop_gain = 80.0f; k.gain_in = 2.0f; k.gain_out = 0.03f; k.pop_k = 100; k.inject_interval = 3;
+        if (cfg.preset == SNN_PRESET_BASELINE) {
+            // the benchmark's constants (C 200 pF, gL 10 nS, EL -70 mV, VT -50 mV,
+            // dT 2 mV, a 2 nS, b 0.08 nA, tau_w 100 ms, dt 1 ms) in the reference's
+            // normalised units: v = (V - EL) / 25 mV (VT -> 0.8, spike at 1), w in
+            // gL * 25 mV; STP U 0.5, tau_d 200, tau_f 50 for every synapse class,
+            // the feed-forward per-step recovery included
+            k.inv_taum = pm_div(1.0f, 20.0f);
+            k.inv_tauw = pm_div(1.0f, 100.0f);
+            k.vt = 0.8f; k.dT = 0.08f; k.a_ad = 0.2f; k.b_ad = 0.32f;
+            for (int q = 0; q < NCLASS; ++q) {
+                k.U[q] = 0.5f;
+                k.fac[q] = snn_expf(pm_div(-1.0f, 50.0f));
+                k.rec[q] = pm_sub(1.0f, snn_expf(pm_div(-1.0f, 200.0f)));
+            }
+            k.rec_ff_step = k.rec[0];
+        }
     }
 
     void set_shard(int32_t r, int32_t w, const void* uid) override {
@@ -1198,7 +1214,7 @@ struct Engine2e : snnb::Engine {
                 packed[x] = (lay.gmeta[g] & 0x7fu) | ((unsigned)lay.gsize[g] << 8) | (lpre << 24);
                 h_gsize[x] = lay.gsize[g];
                 h_gpre[x] = lay.gpre[g];
-                h_gs[x] = make_float4(1.0f, lay.gu0[g], 0.0f, 0.0f);
+                h_gs[x] = make_float4(1.0f, cfg.preset == SNN_PRESET_BASELINE ? 0.5f : lay.gu0[g], 0.0f, 0.0f);
             }
             gmeta.upload(packed.data(), G, stream);
             gsize.upload(h_gsize.data(), G, stream);

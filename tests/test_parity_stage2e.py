@@ -54,11 +54,12 @@ def compare_state(net, orc, tag):
 
 
 def run_pair(ncol, steps, corpus_seed=7, phase_offset=0, e0=False, chunk=None, threads=0,
-             check_state_every=None):
+             check_state_every=None, preset=0):
     corpus = snn.stream(20000, seed=corpus_seed)
     orc = po.Oracle2e(po.ref_params(ncol, e0=int(e0), phase_offset=phase_offset,
-                                    n_threads=threads), corpus)
-    net = snn.Network(e0=e0, phase_offset=phase_offset)
+                                    n_threads=threads, preset=preset), corpus)
+    net = snn.Network(e0=e0, phase_offset=phase_offset,
+                      preset=snn.PRESET_BASELINE if preset else snn.PRESET_REF)
     net.build_columns(snn.topology(n_columns=ncol))
     net.set_corpus(corpus)
     assert (net.N, net.S) == (orc.N, orc.S)
@@ -131,6 +132,13 @@ def test_parity_critical_and_pruning_phases():
 @pytest.mark.gpu
 def test_parity_e0_ablation():
     run_pair(2, 600, e0=True, phase_offset=5000)
+
+
+@pytest.mark.gpu
+def test_parity_baseline_preset():
+    """The benchmark's AdEx / STP constants (SNN_PRESET_BASELINE) in the
+    SYNAPTOGENIC phase, rasters every step and the full state twice."""
+    run_pair(4, 400, phase_offset=5000, chunk=100, check_state_every=200, preset=1)
 
 
 @pytest.mark.gpu
