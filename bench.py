@@ -278,6 +278,80 @@ def prop_main(args):
             net.close()
 
 
+def stage0_main(args):
+    """Configurations 0 and 1 (Stage 0 block network, Stage 2A columnar
+    network), benchmark constants: one JSON line each."""
+    import snn_b200 as snn
+    import torch
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import pyoracle as po
+    warm = max(args.warmup, 3)
+    for columnar in (False, True):
+        name = ("stage2A columnar 10 x 1,000 LIF / 1M synapses, synthetic UTF-8 (p_CJK 0.85)"
+                if columnar else "stage0 10,000 LIF / 1M synapses, uniform random bytes")
+        if columnar:
+            data = snn.stream(1 << 20, seed=STREAM_SEED, p_cjk=0.85)
+        else:
+            data = np.random.default_rng(STREAM_SEED).integers(0, 256, 1 << 20).astype(np.uint8)
+        net = snn.Network(model=snn.MODEL_STAGE0, preset=snn.PRESET_BASELINE)
+        net.build_columns(snn.topology(snn.MODEL_STAGE0, n_columns=10 if columnar else 0))
+        net.set_corpus(data.tobytes())
+        net.run(warm)
+        net.synchronize()
+        c0 = net.counters()
+        net.set_profiling(True)
+        with ClockSampler(0) as clk:
+            net.run(args.steps)
+            net.synchronize()
+        prof = net.profile()
+        net.set_profiling(False)
+        c1 = net.counters()
+        ev = c1["dispatched"] - c0["dispatched"]
+        dev_s = prof["step_ms"] / 1000.0
+        # e2e: the input bytes copied from pinned host memory with the call
+        pin = torch.empty(args.steps, dtype=torch.uint8, pin_memory=True)
+        pin.numpy()[:] = data[: args.steps]
+        ce0 = net.counters()
+        t0 = time.perf_counter()
+        net._check(net.L.snn_run(net.h, args.steps, pin.data_ptr(), args.steps, 1, None, None))
+        net.synchronize()
+        wall = time.perf_counter() - t0
+        e2e_ev = net.counters()["dispatched"] - ce0["dispatched"]
+        line = {
+            "metric": "synaptic events/sec (SOPS) and sim steps/sec, " + name,
+            "value": ev / dev_s, "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": warm,
+            "ms_per_step": prof["step_ms"] / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "steps_per_sec": args.steps / dev_s,
+            "config": {"workload": name, "constants": "benchmark (baseline preset)",
+                       "events_per_step": ev / args.steps,
+                       "l2": "L2-resident (1M synapses)"},
+            "e2e": {"value": e2e_ev / wall, "unit": UNIT, "h2d_bytes_per_step": 1,
+                    "d2h_bytes_per_step": 0, "steps_per_sec": args.steps / wall},
+            "gpu_launches": int(sum(v["launches"] for v in prof["kernels"].values())),
+            "kernels_ms_per_step": {k: v["ms"] / max(v["launches"], 1) for k, v in prof["kernels"].items()},
+            "clocks": clk.summary(),
+        }
+        if not args.no_cpu_baseline:
+            cores = os.cpu_count()
+            o = po.Oracle0(po.stage0_params(columnar=columnar, baseline=True, n_threads=cores))
+            o.run(warm, data[:warm])
+            s0 = o.sizes()
+            t0, n = time.perf_counter(), 0
+            while n < 50 or time.perf_counter() - t0 < 8.0:
+                o.run(10, data[warm + n: warm + n + 10])
+                n += 10
+            dt = time.perf_counter() - t0
+            s1 = o.sizes()
+            deg = int(s1[1] // s1[0])
+            line["cpu_baseline"] = {"value": float(s1[3] - s0[3]) * deg / dt, "unit": UNIT,
+                                    "cores": cores, "kind": "port",
+                                    "sample": f"{n} steps, CPU oracle, {cores} OpenMP threads"}
+            o.close()
+        print(json.dumps(line), flush=True)
+        net.close()
+
+
 def shard_main(args):
     """Configuration 3: the Stage 2e network scaled to --columns columns
     (5,000: 5.5 M neurons / 1.07 B synapses), sharded by column over the
@@ -376,10 +450,11 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=1000)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="stage2e", choices=["stage2e", "prop", "shard"],
+    ap.add_argument("--workload", default="stage2e", choices=["stage2e", "prop", "shard", "stage0"],
                     help="stage2e: the 55k/10.7M network (one line); prop: the 1M x 1,000 "
                          "propagation microbench (one line per mode and rate, 1 GPU); shard: "
-                         "the 100x network column-sharded over the torchrun ranks")
+                         "the 100x network column-sharded over the torchrun ranks; stage0: "
+                         "configurations 0 and 1 (one line each, 1 GPU)")
     ap.add_argument("--columns", type=int, default=5000, help="shard workload: columns")
     ap.add_argument("--prop-neurons", type=int, default=1_000_000)
     ap.add_argument("--prop-rates", default="", help="comma list, default 0.001,0.01,0.03,0.1")
@@ -391,6 +466,9 @@ def main():
         return
     if args.workload == "shard":
         shard_main(args)
+        return
+    if args.workload == "stage0":
+        stage0_main(args)
         return
 
     rank = int(os.environ.get("RANK", "0"))
