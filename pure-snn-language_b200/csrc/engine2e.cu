@@ -56,6 +56,9 @@ constexpr uint32_t GV_D_MASK = 0x1f, GV_FF = 1u << 5, GV_EXC = 1u << 6, GV_ARR =
                    GV_NEXT = 1u << 8, GV_DISP = 1u << 9,
                    GV_EV = 1u << 10;  // arrival, dispatch or a ring read for the next step
 constexpr int NEU_BLOCK = 128;  // k_neurons CTA size; groups carry their pre's index in it
+#ifndef NEU_GU
+#define NEU_GU 4   // groups per thread in flight in k_neurons
+#endif
 // packed static group word: d_eff | ff << 5 | exc << 6 | size << 8 | (pre % NEU_BLOCK) << 24
 __host__ __device__ inline unsigned gw_size(unsigned m) { return (m >> 8) & 0xffffu; }
 __host__ __device__ inline unsigned gw_lpre(unsigned m) { return m >> 24; }
@@ -392,6 +395,21 @@ __global__ void __launch_bounds__(NEU_BLOCK) k_neurons(Dev d, Consts k) {
     const int gi = i < d.n_a ? d.a0 + i : d.pf0 + (i - d.n_a);  // global neuron id
     const int i0 = blockIdx.x * blockDim.x;
     const int i1 = min(i0 + (int)blockDim.x, d.N);
+    const bool valid = i < d.N;
+    // the neuron's state is loaded first: its latency overlaps the step
+    // inputs and gates below
+    struct NeuIn {
+        unsigned info, hist;
+        float input, fr, V, s, nmda, wad, can, xpost;
+        int ref, last;
+        unsigned short off;
+    } nu{};
+    if (valid) {
+        nu.info = d.info[i]; nu.input = d.input[i]; nu.ref = d.ref[i]; nu.fr = d.fr[i];
+        nu.V = d.V[i]; nu.off = d.off[i]; nu.s = d.s[i]; nu.nmda = d.nmda_cur[i];
+        nu.wad = d.wad[i]; nu.can = d.can[i]; nu.xpost = d.xpost[i]; nu.hist = d.hist[i];
+        nu.last = d.last[i];
+    }
     if (threadIdx.x == 0) {
         s_in = step_inputs(d, k);
         if (blockIdx.x == 0) publish_step(d, k, s_in);
@@ -415,14 +433,13 @@ __global__ void __launch_bounds__(NEU_BLOCK) k_neurons(Dev d, Consts k) {
         }
         __syncthreads();
     }
-    const bool valid = i < d.N;
     unsigned spike = 0;
     unsigned hist = 0;
     if (valid) {
-        const unsigned info = d.info[i];
+        const unsigned info = nu.info;
         const int type = info & 1, region = (info >> 1) & 7, subtype = (info >> 4) & 3;
         const int col = (region != PF) ? (int)(info >> 8) : -1;
-        float input = d.input[i];
+        float input = nu.input;
         if (s_in.inject && region == L4) {
             const int off = gi - col * d.NPC;
             const int b = s_in.byte;
@@ -439,7 +456,7 @@ __global__ void __launch_bounds__(NEU_BLOCK) k_neurons(Dev d, Consts k) {
         if (c->inh_active) {
             const float sg = subtype == 0 ? 1.40f : subtype == 1 ? 0.85f : subtype == 2 ? 1.10f : 1.0f;
             const float rg = region == PF ? 0.60f : 1.0f;
-            float cur = pm_mul(pm_mul(pm_fma(d.fr[i], 2.0f, c->gdrive), sg), rg);
+            float cur = pm_mul(pm_mul(pm_fma(nu.fr, 2.0f, c->gdrive), sg), rg);
             if (type == 1) cur = pm_mul(cur, 0.35f);
             if (cur > 2.0f) cur = 2.0f;
             inh = cur;
@@ -456,17 +473,17 @@ __global__ void __launch_bounds__(NEU_BLOCK) k_neurons(Dev d, Consts k) {
                 }
             }
         }
-        int ref = d.ref[i];
-        float fr = d.fr[i];
-        float V = d.V[i];
-        unsigned short off = d.off[i];
+        int ref = nu.ref;
+        float fr = nu.fr;
+        float V = nu.V;
+        unsigned short off = nu.off;
         if (ref > 0) {
             d.ref[i] = ref - 1;
             d.fr[i] = pm_mul(fr, k.fr_refr);
         } else {
-            const float s = pm_fma(d.s[i], k.syn_keep, pm_mul(input, k.syn_in));
-            const float I = pm_sub(pm_add(s, d.nmda_cur[i]), inh);
-            float w = d.wad[i];
+            const float s = pm_fma(nu.s, k.syn_keep, pm_mul(input, k.syn_in));
+            const float I = pm_sub(pm_add(s, nu.nmda), inh);
+            float w = nu.wad;
             float ea = pm_div(pm_sub(V, k.vt), k.dT);
             if (ea > 10.0f) ea = 10.0f;
             if (ea < -10.0f) ea = -10.0f;
@@ -477,10 +494,10 @@ __global__ void __launch_bounds__(NEU_BLOCK) k_neurons(Dev d, Consts k) {
             w = pm_add(w, dw);
             V = clampf(V, k.vmin, k.vmax);
             const float theta = pm_add(1.0f, pm_div(pm_u2f(off), 256.0f));
-            float can = d.can[i];
+            float can = nu.can;
             if (V >= theta) {
                 spike = 1;
-                const int last = d.last[i];
+                const int last = nu.last;
                 if (last >= 0 && t - last <= 5) atomicAdd(&d.ctrl->burst, 1ull);
                 d.last[i] = (int)t;
                 ref = k.refr_steps;
@@ -508,10 +525,10 @@ __global__ void __launch_bounds__(NEU_BLOCK) k_neurons(Dev d, Consts k) {
         const float Vb = pm_fma(50.0f, V, -70.0f);
         const float e = snn_expf(pm_div(-Vb, 16.13f));
         d.mg[i] = pm_div(1.0f, pm_add(1.0f, pm_div(pm_mul(1.0f, e), 3.57f)));
-        float xp = pm_mul(d.xpost[i], k.dec_xpost);
+        float xp = pm_mul(nu.xpost, k.dec_xpost);
         if (spike) xp = pm_add(xp, k.a_minus);
         d.xpost[i] = xp;
-        hist = (d.hist[i] << 1) | spike;
+        hist = (nu.hist << 1) | spike;
         d.hist[i] = hist;
         if (spike) {
             const int sub = gi / d.per_sub;
@@ -547,16 +564,22 @@ __global__ void __launch_bounds__(NEU_BLOCK) k_neurons(Dev d, Consts k) {
     auto group_update = [&](int g, unsigned meta, float4 st) {
         update_group(d, k, g, meta, st, s_hist[gw_lpre(meta)], t, arr_cnt, disp_cnt);
     };
-    // two groups per iteration keep independent loads in flight
-    const int stride = 2 * blockDim.x;
+    // NEU_GU groups per iteration keep independent loads in flight
+    const int stride = NEU_GU * blockDim.x;
     for (int g = g0 + (int)threadIdx.x; g < g1; g += stride) {
-        const int g2 = g + blockDim.x;
-        const unsigned m0 = d.gmeta[g];
-        const unsigned m1 = g2 < g1 ? d.gmeta[g2] : 0u;
-        const float4 s0 = d.gstate[g];
-        const float4 s1 = g2 < g1 ? d.gstate[g2] : make_float4(0, 0, 0, 0);
-        group_update(g, m0, s0);
-        if (g2 < g1) group_update(g2, m1, s1);
+        unsigned m[NEU_GU];
+        float4 st[NEU_GU];
+#pragma unroll
+        for (int u = 0; u < NEU_GU; ++u) {
+            const int gu = g + u * (int)blockDim.x;
+            m[u] = gu < g1 ? d.gmeta[gu] : 0u;
+            st[u] = gu < g1 ? d.gstate[gu] : make_float4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < NEU_GU; ++u) {
+            const int gu = g + u * (int)blockDim.x;
+            if (gu < g1) group_update(gu, m[u], st[u]);
+        }
     }
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) {
