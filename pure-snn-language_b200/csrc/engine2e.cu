@@ -890,6 +890,13 @@ __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d,
         const int buf = it & 1;
         const int next = j + W;
         if (lane == 0 && next < d.N) issue(next, buf ^ 1);
+        // this neuron's row bounds and scalars, issued before the wait so that
+        // their latency overlaps the staging copy
+        const int b = d.in_ptr[j], e = d.in_ptr[j + 1];
+        pc.mgj = d.mg[j];
+        const unsigned hist_j = d.hist[j];
+        pc.xpost = d.xpost[j];
+        const float V_j = d.V[j];
         bool ok = false;
         for (unsigned spin = 0; spin < WAIT_LIMIT; ++spin) {
             if (mbar_try_wait(&bar[buf], (phases >> buf) & 1u)) { ok = true; break; }
@@ -904,14 +911,11 @@ __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d,
             }
             return;
         }
-        const int b = d.in_ptr[j], e = d.in_ptr[j + 1];
         const int a0 = b & ~3;
         const unsigned* sg = wbase + 2 * cap * buf;
         float* sc = reinterpret_cast<float*>(wbase + 2 * cap * buf + cap);
-        pc.mgj = d.mg[j];
-        pc.post_spk = d.hist[j] & 1u;
-        pc.xpost = d.xpost[j];
-        pc.one_m_V = pm_sub(k.e_rev, d.V[j]);
+        pc.post_spk = hist_j & 1u;
+        pc.one_m_V = pm_sub(k.e_rev, V_j);
         const bool all = all_events || pc.post_spk;
         float part_nmda = 0.0f, part_in = 0.0f;
         int qn = 0;
