@@ -1,7 +1,7 @@
 // engine2e.cu - Stage 2e engine on sm_100a: AdEx neurons, NMDA/Ca synapses,
 // Tsodyks-Markram STP, dual-trace PSW STDP, CaMKII / eligibility, axonal
 // delays, thalamic gate, modulators and inhibition, one step = 2 kernels
-// (+ the all-gather and k_mirror between them on column shards):
+// (+ the all-gather and the mirror-group kernels between them on column shards):
 //
 //   k_neurons   (N threads) start of step t (byte, phase gain, M_ij, thalamic
 //                           gates), population-coded input, inhibition, AdEx update,
@@ -140,9 +140,9 @@ struct Dev {
     // column sharding: local neuron j is global a0 + j for j < n_a, else
     // pf0 + (j - n_a).  With sharded != 0 the step's spike words, spike count
     // and TD sub-population counts go to `send`, every rank's payload arrives
-    // in `recv` (an all-gather between k_neurons and k_mirror), and the
+    // in `recv` (an all-gather between k_neurons and k_mirror_hist), and the
     // groups of remote pres ("mirror" groups, after the local ones) are
-    // updated by k_mirror from the gathered bits.
+    // updated by k_mirror_groups from the gathered bits.
     int n_a, a0, pf0, sharded, world;
     int c0, c1;             // this rank's columns
     unsigned* send;
@@ -152,6 +152,8 @@ struct Dev {
     const int* mbeg;        // M + 1 group ranges
     const unsigned* mbit;   // bit of each mirror pre in recv
     unsigned* mhist;        // 32-step spike history of each mirror pre
+    long long G_local, GM;  // groups of local pres; mirror groups (after them)
+    const int* gmir;        // mirror pre of each mirror group
 };
 
 __device__ __forceinline__ int phase_of(long long step) {
@@ -532,7 +534,7 @@ __global__ void __launch_bounds__(NEU_BLOCK) k_neurons(Dev d, Consts k) {
         d.hist[i] = hist;
         if (spike) {
             const int sub = gi / d.per_sub;
-            if (d.sharded) {  // global counts are summed over the ranks by k_mirror
+            if (d.sharded) {  // global counts are summed over the ranks by k_mirror_hist
                 atomicAdd(&d.send[d.words_max], 1u);
                 if (sub < TD_DIM) atomicAdd(&d.send[d.words_max + 1 + sub], 1u);
             } else {
@@ -596,13 +598,15 @@ __global__ void __launch_bounds__(NEU_BLOCK) k_neurons(Dev d, Consts k) {
 }
 
 // ---------------------------------------------------------------------------
-// k_mirror (sharded runs): after the all-gather of step t's payloads, the
-// global spike count and TD sub-population counts of step t (block 0), then
-// one thread per mirror pre: its history gains the gathered bit of step t and
-// its groups (synapses onto this rank's neurons) get the same update the
-// owning rank's k_neurons gives a local pre's groups.
+// Sharded runs, after the all-gather of step t's payloads:
+//   k_mirror_hist   block 0: the global spike count and TD sub-population
+//                   counts of step t; one thread per mirror pre (remote pre
+//                   with synapses onto this rank): its 32-step history gains
+//                   the gathered bit of step t
+//   k_mirror_groups one thread per mirror group: the update the owning rank's
+//                   k_neurons gives a local pre's groups
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(NEU_BLOCK) k_mirror(Dev d, Consts k) {
+__global__ void __launch_bounds__(256) k_mirror_hist(Dev d) {
     const long long t = d.ctrl->t;
     if (blockIdx.x == 0) {
         if (threadIdx.x == 0) {
@@ -617,13 +621,19 @@ __global__ void __launch_bounds__(NEU_BLOCK) k_mirror(Dev d, Consts k) {
         }
     }
     const int m = blockIdx.x * blockDim.x + threadIdx.x;
-    unsigned long long arr_cnt = 0, disp_cnt = 0;
     if (m < d.M) {
         const unsigned b = d.mbit[m];
-        const unsigned h = (d.mhist[m] << 1) | ((d.recv[b >> 5] >> (b & 31)) & 1u);
-        d.mhist[m] = h;
-        const int ge = d.mbeg[m + 1];
-        for (int g = d.mbeg[m]; g < ge; ++g) update_group(d, k, g, d.gmeta[g], d.gstate[g], h, t, arr_cnt, disp_cnt);
+        d.mhist[m] = (d.mhist[m] << 1) | ((d.recv[b >> 5] >> (b & 31)) & 1u);
+    }
+}
+
+__global__ void __launch_bounds__(256) k_mirror_groups(Dev d, Consts k) {
+    const long long t = d.ctrl->t;
+    const long long x = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    unsigned long long arr_cnt = 0, disp_cnt = 0;
+    if (x < d.GM) {
+        const int g = (int)(d.G_local + x);
+        update_group(d, k, g, d.gmeta[g], d.gstate[g], d.mhist[d.gmir[x]], t, arr_cnt, disp_cnt);
     }
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) {
@@ -1051,7 +1061,7 @@ struct Engine2e : snnb::Engine {
     Shard sh;
     std::vector<int64_t> new_of_old;  // layout group id -> device group id
     snnb::DevBuf<unsigned> send, recv, mbit, mhist;
-    snnb::DevBuf<int> mbeg;
+    snnb::DevBuf<int> mbeg, gmir;
     int64_t G_local = 0;              // groups of local pres (the rest mirror remote pres)
 
     explicit Engine2e(const snn_config& c) : cfg(c) {
@@ -1258,6 +1268,16 @@ struct Engine2e : snnb::Engine {
         if (!h_mbit.empty()) mbit.upload(h_mbit.data(), h_mbit.size(), stream);
         mhist.alloc(std::max<size_t>(h_mbit.size(), 1));
         mhist.zero(stream);
+        {   // mirror pre of every mirror group
+            std::vector<int> h_gmir((size_t)std::max<int64_t>(G - G_local, 1), 0);
+            for (size_t m = 0; m + 1 < h_mbeg.size(); ++m)
+                for (int g = h_mbeg[m]; g < h_mbeg[m + 1]; ++g) h_gmir[(size_t)(g - G_local)] = (int)m;
+            gmir.alloc(h_gmir.size());
+            gmir.upload(h_gmir.data(), h_gmir.size(), stream);
+            SNN_CUDA(cudaStreamSynchronize(stream));
+        }
+        D.G_local = G_local;
+        D.GM = G - G_local;
         if (world > 1) {
             send.alloc(pw);
             send.zero(stream);
@@ -1341,6 +1361,7 @@ struct Engine2e : snnb::Engine {
         D.neuron_byte_counts = neuron_byte_counts.p; D.w_value = w_value.p; D.w_pred = w_pred.p;
         D.baseline = baseline.p; D.corpus = corpus.p; D.raster = raster.p;
         D.send = send.p; D.recv = recv.p; D.mbeg = mbeg.p; D.mbit = mbit.p; D.mhist = mhist.p;
+        D.gmir = gmir.p;
     }
 
     void set_corpus(const uint8_t* b, int64_t n) override {
@@ -1386,7 +1407,8 @@ struct Engine2e : snnb::Engine {
         if (world > 1) {
             const ncclResult_t nr = ncclAllGather(send.p, recv.p, (size_t)D.pw, ncclUint32, comm, st);
             SNN_REQUIRE(nr == ncclSuccess, SNN_ERR_CUDA, std::string("ncclAllGather: ") + ncclGetErrorString(nr));
-            k_mirror<<<std::max(1, (D.M + NEU_BLOCK - 1) / NEU_BLOCK), NEU_BLOCK, 0, st>>>(D, K);
+            k_mirror_hist<<<std::max(1, (D.M + 255) / 256), 256, 0, st>>>(D);
+            k_mirror_groups<<<(unsigned)std::max(1ll, (D.GM + 255) / 256), 256, 0, st>>>(D, K);
             if (ev) SNN_CUDA(cudaEventRecordWithFlags(ev[e++], st, fl));
         }
         k_synapses<<<syn_grid, SYN_THREADS, syn_smem, st>>>(D, K);
@@ -1451,7 +1473,7 @@ struct Engine2e : snnb::Engine {
         memset(&prof, 0, sizeof(prof));
         int q = 0;
         strcpy(prof.names[q++], "k_neurons");
-        if (world > 1) strcpy(prof.names[q++], "allgather+k_mirror");
+        if (world > 1) strcpy(prof.names[q++], "allgather+mirror");
         strcpy(prof.names[q++], "k_synapses");
         strcpy(prof.names[q++], "k_synapses@t%10==0");
         prof.n_kernels = q;
