@@ -333,15 +333,16 @@ __device__ void step_epilogue(const Dev& d, const Consts& k) {
 // STP / NMDA / pre-trace update of group g at step t from its pre's spike
 // history h (bit 0 = spike at t, bit d = spike at t - d) and its per-step
 // view for the synapse pass
+// (ex = the group's AMPA conductance and last arrival step, loaded by the
+// caller together with meta and st)
 __device__ __forceinline__ void update_group(const Dev& d, const Consts& k, int g, unsigned meta, float4 st,
-                                             unsigned h, long long t, unsigned long long& arr_cnt,
-                                             unsigned long long& disp_cnt) {
+                                             float2 ex, unsigned h, long long t,
+                                             unsigned long long& arr_cnt, unsigned long long& disp_cnt) {
     const int dd = meta & GV_D_MASK;
     const bool ff = meta & GV_FF, exc = meta & GV_EXC;
     const bool arr = (h >> dd) & 1u;
     const bool nxt = (h >> (dd - 1)) & 1u;
     const bool disp = h & 1u;
-    float2 ex = d.gextra[g];  // AMPA (all receptor classes) and the last arrival
     if (arr) {
         ex.x = pm_fma(pm_mul(1.0f, st.x), st.y, ex.x);
         ex.y = pm_ll2f(t);
@@ -412,6 +413,11 @@ __global__ void __launch_bounds__(NEU_BLOCK) k_neurons(Dev d, Consts k) {
         nu.wad = d.wad[i]; nu.can = d.can[i]; nu.xpost = d.xpost[i]; nu.hist = d.hist[i];
         nu.last = d.last[i];
     }
+    // the CTA's group range and the inhibition scalars (written by the
+    // previous step's epilogue, not modified in this kernel)
+    const int g0 = d.gbeg[i0], g1 = d.gbeg[i1];
+    const int inh_active = c->inh_active, kwta_k = c->kwta_k;
+    const float gdrive = c->gdrive;
     if (threadIdx.x == 0) {
         s_in = step_inputs(d, k);
         if (blockIdx.x == 0) publish_step(d, k, s_in);
@@ -455,16 +461,16 @@ __global__ void __launch_bounds__(NEU_BLOCK) k_neurons(Dev d, Consts k) {
             }
         }
         float inh = 0.0f;
-        if (c->inh_active) {
+        if (inh_active) {
             const float sg = subtype == 0 ? 1.40f : subtype == 1 ? 0.85f : subtype == 2 ? 1.10f : 1.0f;
             const float rg = region == PF ? 0.60f : 1.0f;
-            float cur = pm_mul(pm_mul(pm_fma(nu.fr, 2.0f, c->gdrive), sg), rg);
+            float cur = pm_mul(pm_mul(pm_fma(nu.fr, 2.0f, gdrive), sg), rg);
             if (type == 1) cur = pm_mul(cur, 0.35f);
             if (cur > 2.0f) cur = 2.0f;
             inh = cur;
             if (col >= 0) {
                 const int sp = d.col_sp[((t - 1) & 1) * d.ncol + col];
-                const int kk = c->kwta_k;
+                const int kk = kwta_k;
                 int width = kk * 8;
                 width = width < 1 ? 1 : (width > d.NPC ? d.NPC : width);
                 const int rank = (gi + col * 37) % d.NPC;
@@ -561,26 +567,26 @@ __global__ void __launch_bounds__(NEU_BLOCK) k_neurons(Dev d, Consts k) {
     }
     __syncthreads();
     // outgoing synapse groups of this CTA's neurons, one thread per group
-    const int g0 = d.gbeg[i0], g1 = d.gbeg[i1];
     unsigned long long arr_cnt = 0, disp_cnt = 0;
-    auto group_update = [&](int g, unsigned meta, float4 st) {
-        update_group(d, k, g, meta, st, s_hist[gw_lpre(meta)], t, arr_cnt, disp_cnt);
-    };
-    // NEU_GU groups per iteration keep independent loads in flight
+    // NEU_GU groups per iteration: every load of the iteration is issued
+    // before the first group's stores
     const int stride = NEU_GU * blockDim.x;
     for (int g = g0 + (int)threadIdx.x; g < g1; g += stride) {
         unsigned m[NEU_GU];
         float4 st[NEU_GU];
+        float2 ex[NEU_GU];
 #pragma unroll
         for (int u = 0; u < NEU_GU; ++u) {
             const int gu = g + u * (int)blockDim.x;
             m[u] = gu < g1 ? d.gmeta[gu] : 0u;
             st[u] = gu < g1 ? d.gstate[gu] : make_float4(0, 0, 0, 0);
+            ex[u] = gu < g1 ? d.gextra[gu] : make_float2(0, 0);
         }
 #pragma unroll
         for (int u = 0; u < NEU_GU; ++u) {
             const int gu = g + u * (int)blockDim.x;
-            if (gu < g1) group_update(gu, m[u], st[u]);
+            if (gu < g1)
+                update_group(d, k, gu, m[u], st[u], ex[u], s_hist[gw_lpre(m[u])], t, arr_cnt, disp_cnt);
         }
     }
 #pragma unroll
@@ -633,7 +639,8 @@ __global__ void __launch_bounds__(256) k_mirror_groups(Dev d, Consts k) {
     unsigned long long arr_cnt = 0, disp_cnt = 0;
     if (x < d.GM) {
         const int g = (int)(d.G_local + x);
-        update_group(d, k, g, d.gmeta[g], d.gstate[g], d.mhist[d.gmir[x]], t, arr_cnt, disp_cnt);
+        update_group(d, k, g, d.gmeta[g], d.gstate[g], d.gextra[g], d.mhist[d.gmir[x]], t, arr_cnt,
+                     disp_cnt);
     }
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) {
