@@ -38,6 +38,7 @@ struct Args {        // per launch
 
 struct Ctrl {
     unsigned long long spikes, events;
+    unsigned long long step_events[2];  // outgoing synapses of the step's spikes (by step parity)
     int step_spikes[2];
     long long raster_base;
     int reset_pending;
@@ -147,6 +148,7 @@ __global__ void __launch_bounds__(256) k0_prop_lif(Dev d, Consts k, int kstep) {
         atomicAdd(&d.ctrl->spikes, 1ull);
         atomicAdd(&d.ctrl->events, (unsigned long long)d.outdeg[j]);
         atomicAdd(&d.ctrl->step_spikes[t & 1], 1);
+        atomicAdd(&d.ctrl->step_events[t & 1], (unsigned long long)d.outdeg[j]);
         const long long row = (t - d.ctrl->raster_base) % d.raster_cap;
         atomicOr(&d.raster[row * d.words + (j >> 5)], 1u << (j & 31));
     }
@@ -169,10 +171,14 @@ __global__ void __launch_bounds__(256) k0_stdp(Dev d, Consts k, int kstep) {
     const int j = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const Args& a = *d.args;
     const long long t = a.t0 + kstep;
-    // clear the raster row of the next step and this step's reset flag
+    // clear the raster row and the spike / event counts of the next step
     if (blockIdx.x == 0) {
         const long long row = (t + 1 - d.ctrl->raster_base) % d.raster_cap;
         for (int q = threadIdx.x; q < d.words; q += blockDim.x) d.raster[row * d.words + q] = 0u;
+        if (threadIdx.x == 0) {
+            d.ctrl->step_spikes[(t + 1) & 1] = 0;
+            d.ctrl->step_events[(t + 1) & 1] = 0ull;
+        }
     }
     if (j >= d.N) return;
     const unsigned char* snow = d.spk + (t & 1) * (long long)d.N;
@@ -246,6 +252,7 @@ struct Engine0 : snnb::Engine {
     float dopamine = 1.0f;
     int reset_interval = 0;
     std::vector<int32_t> h_pre, h_post, perm, in_ptr_h;  // perm: post-major -> generation id
+    std::vector<int32_t> out_ptr_h;  // pre-major row pointer of the generation order
     std::vector<uint8_t> h_type;
     snnb::DevBuf<float> V, I, fr, A, B, input, w, e, exp_tab;
     snnb::DevBuf<int> ref, last, off, in_ptr, outdeg;
@@ -347,6 +354,8 @@ struct Engine0 : snnb::Engine {
             pm_w[pos] = h_w[s];
         }
         std::vector<int> h_outdeg(N, deg);
+        out_ptr_h.resize((size_t)N + 1);
+        for (int i = 0; i <= N; ++i) out_ptr_h[i] = i * deg;
         // device
         V.alloc(N); I.alloc(N); fr.alloc(N); A.alloc(N); B.alloc(N); input.alloc(N);
         ref.alloc(N); last.alloc(N); off.alloc(N); info.alloc(N); spk.alloc(2 * (size_t)N);
@@ -515,7 +524,8 @@ struct Engine0 : snnb::Engine {
         o->step = steps;
         o->total_spikes = (int64_t)h.spikes;
         o->dispatched = (int64_t)h.events;
-        o->arrivals = (int64_t)h.events - (steps > 0 ? (int64_t)h.step_spikes[(steps - 1) & 1] * (S / N) : 0);
+        // the last step's dispatches arrive at the next step
+        o->arrivals = (int64_t)h.events - (steps > 0 ? (int64_t)h.step_events[(steps - 1) & 1] : 0);
         o->n_neurons = N;
         o->n_synapses = S;
         o->last_spikes = steps > 0 ? h.step_spikes[(steps - 1) & 1] : 0;
@@ -557,14 +567,10 @@ struct Engine0 : snnb::Engine {
             case SNN_STATE_WEIGHT: syn(w); break;
             case SNN_STATE_ELIG: syn(e); break;
             case SNN_STATE_POST: need(S * 4); memcpy(buf, h_post.data(), S * 4); break;
-            case SNN_STATE_ROW_PTR: {
-                // pre-major row pointer of the generation order
+            case SNN_STATE_ROW_PTR:  // pre-major row pointer of the generation order
                 need((int64_t)(N + 1) * 4);
-                int32_t* o = (int32_t*)buf;
-                const int deg = (int)(S / N);
-                for (int i = 0; i <= N; ++i) o[i] = i * deg;
+                memcpy(buf, out_ptr_h.data(), (size_t)(N + 1) * 4);
                 break;
-            }
             default: throw snnb::Error(SNN_ERR_UNSUPPORTED, "state field not available for stage0");
         }
     }
@@ -615,6 +621,39 @@ struct Engine0 : snnb::Engine {
         float w, delay, last_pre, last_post, elig, pad;
     };
     static_assert(sizeof(Syn32) == 32, "Synapse record");
+    // Replace the synapse topology by a post-major CSR (row pointer rp[N+1],
+    // pre index col[S]) read from a checkpoint; the caller has checked that
+    // rp starts at 0, ends at S and ascends and that every col is in [0, N).
+    // Generation order of the adopted synapses: by pre, and within a pre by
+    // CSR position.
+    void adopt_topology(const std::vector<int32_t>& rp, const std::vector<int32_t>& col) {
+        std::vector<int32_t> optr((size_t)N + 1, 0);
+        for (int64_t p = 0; p < S; ++p) optr[col[p] + 1]++;
+        std::vector<int> h_outdeg(N);
+        for (int i = 0; i < N; ++i) {
+            h_outdeg[i] = optr[i + 1];
+            optr[i + 1] += optr[i];
+        }
+        std::vector<int32_t> fill(optr.begin(), optr.end() - 1), np((size_t)S), npre((size_t)S), npost((size_t)S);
+        std::vector<unsigned> pm_pre((size_t)S);
+        for (int j = 0; j < N; ++j)
+            for (int32_t p = rp[j]; p < rp[j + 1]; ++p) {
+                const int32_t q = col[p], g = fill[q]++;
+                np[p] = g;
+                npre[g] = q;
+                npost[g] = j;
+                pm_pre[p] = (unsigned)q | ((unsigned)h_type[q] << 31);
+            }
+        in_ptr.upload(rp.data(), N + 1, stream);
+        outdeg.upload(h_outdeg.data(), N, stream);
+        pre.upload(pm_pre.data(), S, stream);
+        SNN_CUDA(cudaStreamSynchronize(stream));
+        in_ptr_h = rp;
+        out_ptr_h = optr;
+        perm = np;
+        h_pre = npre;
+        h_post = npost;
+    }
     void save(const char* path, int32_t fmt) override {
         SNN_REQUIRE(built, SNN_ERR_STATE, "build the network first");
         SNN_CUDA(cudaStreamSynchronize(stream));
@@ -688,8 +727,10 @@ struct Engine0 : snnb::Engine {
         SNN_REQUIRE(fmt == SNN_FMT_SNN2_V1, SNN_ERR_UNSUPPORTED,
                     "Stage 0 reads the native, SNN2 v1 and raw formats");
         // src/stage2/unsupervised_trainer.cu:264-348: header, sizes, then the
-        // synapse records (their weight, eligibility and spike times); the
-        // CSR must be this network's
+        // synapse records (their weight, eligibility and spike times) and
+        // the CSR, which replaces this network's when it differs (a file
+        // written by another build of the same sizes: neuron count, synapse
+        // count; the neuron types stay this network's)
         snnb::BinFile f(path, false);
         SNN_REQUIRE(f.size() >= 32, SNN_ERR_IO, "truncated SNN2 file");
         SNN_REQUIRE(f.get_v<uint32_t>() == 0x534E4E32u, SNN_ERR_IO, "not an SNN2 file (bad magic)");
@@ -707,10 +748,19 @@ struct Engine0 : snnb::Engine {
         std::vector<unsigned> hp((size_t)S);
         pre.download(hp.data(), S, stream);
         SNN_CUDA(cudaStreamSynchronize(stream));
-        SNN_REQUIRE(rp == in_ptr_h, SNN_ERR_IO, "SNN2 row pointer differs from this network");
+        // the CSR spans the synapses, every pre is a neuron, and every
+        // record agrees with the CSR it comes with (checked before any use)
+        SNN_REQUIRE(rp[0] == 0 && rp[N] == (int32_t)S, SNN_ERR_IO, "SNN2 row pointer does not span the synapses");
+        for (int j = 0; j < N; ++j) SNN_REQUIRE(rp[j] <= rp[j + 1], SNN_ERR_IO, "SNN2 row pointer not ascending");
         for (int64_t p = 0; p < S; ++p)
-            SNN_REQUIRE(col[p] == (int32_t)(hp[p] & 0x7fffffffu), SNN_ERR_IO,
-                        "SNN2 column index differs from this network");
+            SNN_REQUIRE(col[p] >= 0 && col[p] < N, SNN_ERR_IO, "SNN2 column index out of range");
+        for (int j = 0; j < N; ++j)
+            for (int32_t p = rp[j]; p < rp[j + 1]; ++p)
+                SNN_REQUIRE(aos[p].post == j && aos[p].pre == col[p], SNN_ERR_IO,
+                            "SNN2 synapse records disagree with the CSR");
+        bool same = rp == in_ptr_h;
+        for (int64_t p = 0; same && p < S; ++p) same = col[p] == (int32_t)(hp[p] & 0x7fffffffu);
+        if (!same) adopt_topology(rp, col);
         std::vector<float> hw((size_t)S), he((size_t)S), hA((size_t)N, -1000.0f);
         for (int64_t p = 0; p < S; ++p) {
             hw[p] = aos[p].w;

@@ -111,6 +111,65 @@ def test_stage0_native_resume_and_snn2_raw_round_trip(tmp_path):
 
 
 @pytest.mark.gpu
+def test_stage0_snn2_adopts_the_files_topology(tmp_path):
+    """An SNN2 file written by a network of the same sizes but another CSR
+    (another topology seed): loading adopts the file's CSR, and the run goes
+    on exactly as on a network built with that topology; a file whose CSR is
+    malformed is refused before anything changes."""
+    corpus = bytes(np.random.default_rng(3).integers(0, 256, 5000).astype(np.uint8))
+
+    def make(seed):
+        net = snn.Network(model=snn.MODEL_STAGE0, preset=snn.PRESET_REF)
+        net.build_columns(snn.topology(snn.MODEL_STAGE0, n_columns=10, seed=seed))
+        net.set_corpus(corpus)
+        return net
+
+    a = make(1)
+    a.run(250)
+    path = str(tmp_path / "a.snn2")
+    a.save(path, snn.FMT_SNN2_V1)
+    same, other = make(1), make(9)
+    assert not np.array_equal(same.state("post"), other.state("post"))
+    v0 = other.state("V").copy()
+    # malformed CSR (a row pointer beyond the synapse count): refused, nothing changed
+    blob = bytearray(open(path, "rb").read())
+    rp_off = 32 + 32 * a.S
+    bad = blob[:]
+    bad[rp_off + 4 * 5: rp_off + 4 * 6] = np.int32(a.S + 10).tobytes()
+    bad_path = str(tmp_path / "bad.snn2")
+    open(bad_path, "wb").write(bytes(bad))
+    with pytest.raises(snn.SnnError) as e:
+        other.load(bad_path, snn.FMT_SNN2_V1)
+    assert e.value.code == ERR_IO
+    assert np.array_equal(bits(other.state("V")), bits(v0))
+    assert other.counters()["step"] == 0
+
+    for n in (same, other):
+        n.load(path, snn.FMT_SNN2_V1)
+    r1, c1 = same.run(150, raster=True, counts=True)
+    r2, c2 = other.run(150, raster=True, counts=True)
+    assert np.array_equal(r1, r2) and c1.sum() > 0
+
+    def edges(n):
+        rp = n.state("row_ptr")
+        pre = np.repeat(np.arange(n.N), np.diff(rp))
+        post, w = n.state("post"), bits(n.state("weight"))
+        o = np.lexsort((w, post, pre))
+        return pre[o], post[o], w[o]
+
+    for x, y in zip(edges(same), edges(other)):
+        assert np.array_equal(x, y)
+    k1, k2 = same.counters(), other.counters()
+    for key in ("step", "total_spikes", "arrivals", "dispatched", "last_spikes"):
+        assert k1[key] == k2[key], key
+    assert k2["last_spikes"] == c2[-1]
+    p1, p2 = str(tmp_path / "s.snn2"), str(tmp_path / "o.snn2")
+    same.save(p1, snn.FMT_SNN2_V1)
+    other.save(p2, snn.FMT_SNN2_V1)
+    assert open(p1, "rb").read() == open(p2, "rb").read()
+
+
+@pytest.mark.gpu
 def test_microbench_native_resume(tmp_path):
     def make():
         n = snn.Network(model=snn.MODEL_PROP, prop_mode=3, prop_rate=0.02)

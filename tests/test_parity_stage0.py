@@ -43,6 +43,11 @@ def run_pair(columnar, baseline, steps, bytes_, chunk=None, dopamine=None):
     assert np.array_equal(bits(net.state("elig")), bits(orc.synapse("elig"))), "eligibility"
     c = net.counters()
     assert c["total_spikes"] == int(orc.sizes()[3])
+    # the last step's spike count, and the arrivals: every dispatch but the last step's
+    assert c["last_spikes"] == int(orc.sizes()[4]) == counts[-1]
+    deg = net.S // net.N
+    assert c["dispatched"] == c["total_spikes"] * deg
+    assert c["arrivals"] == (c["total_spikes"] - c["last_spikes"]) * deg
     net.close()
     orc.close()
 
