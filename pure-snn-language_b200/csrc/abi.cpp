@@ -4,6 +4,7 @@
 #include <memory>
 #include <string>
 #include <nccl.h>
+#include "nccl_dl.h"
 #include "common.h"
 #include "net2e.h"
 
@@ -222,14 +223,20 @@ int snn_load(snn_ctx* ctx, const char* path, int32_t fmt) {
 
 int snn_nccl_unique_id(uint8_t* out, int64_t n) {
     if (!out || n < (int64_t)sizeof(ncclUniqueId)) return SNN_ERR_ARG;
-    ncclUniqueId id;
-    const ncclResult_t r = ncclGetUniqueId(&id);
-    if (r != ncclSuccess) {
-        g_create_err = std::string("ncclGetUniqueId: ") + ncclGetErrorString(r);
-        return SNN_ERR_CUDA;
+    try {
+        const snnb::NcclApi& nc = snnb::nccl();
+        ncclUniqueId id;
+        const ncclResult_t r = nc.GetUniqueId(&id);
+        if (r != ncclSuccess) {
+            g_create_err = std::string("ncclGetUniqueId: ") + nc.GetErrorString(r);
+            return SNN_ERR_CUDA;
+        }
+        memcpy(out, &id, sizeof(id));
+        return SNN_OK;
+    } catch (const snnb::Error& e) {
+        g_create_err = e.what();
+        return e.code;
     }
-    memcpy(out, &id, sizeof(id));
-    return SNN_OK;
 }
 
 int snn_set_shard(snn_ctx* ctx, int32_t rank, int32_t world, const uint8_t* uid, int64_t n) {

@@ -40,6 +40,7 @@
 #include <cstdio>
 #include <memory>
 #include <nccl.h>
+#include "nccl_dl.h"
 #include "ckpt.h"
 #include "common.h"
 #include "net2e.h"
@@ -604,13 +605,21 @@ __global__ void __launch_bounds__(NEU_BLOCK) k_neurons(Dev d, Consts k) {
 }
 
 // ---------------------------------------------------------------------------
-// Sharded runs, after the all-gather of step t's payloads:
-//   k_mirror_hist   block 0: the global spike count and TD sub-population
-//                   counts of step t; one thread per mirror pre (remote pre
-//                   with synapses onto this rank): its 32-step history gains
-//                   the gathered bit of step t
-//   k_mirror_groups one thread per mirror group: the update the owning rank's
-//                   k_neurons gives a local pre's groups
+// Sharded runs.  A mirror group (the groups of a remote pre with synapses onto
+// this rank) is updated in two parts, which together give exactly the update
+// the owning rank's k_neurons gives a local pre's groups:
+//   k_mirror_groups  one thread per mirror group, before step t's exchange
+//                    (on a side stream, overlapping k_neurons and the
+//                    all-gather): the update from the pre's spikes up to
+//                    t - 1, i.e. with bit 0 (a spike at t) still clear.  Only
+//                    the dispatch flag and, for delay 1, the next-step flag
+//                    depend on bit 0.
+//   k_mirror_hist    after the all-gather of step t's payloads: block 0 sums
+//                    the global spike count and TD sub-population counts of
+//                    step t; one thread per mirror pre shifts the gathered bit
+//                    of step t into its 32-step history and, if the pre spiked,
+//                    sets the dispatch (and delay-1 next-step) flags of its
+//                    mirror groups and counts their dispatches.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) k_mirror_hist(Dev d) {
     const long long t = d.ctrl->t;
@@ -627,32 +636,42 @@ __global__ void __launch_bounds__(256) k_mirror_hist(Dev d) {
         }
     }
     const int m = blockIdx.x * blockDim.x + threadIdx.x;
+    unsigned long long disp_cnt = 0;
     if (m < d.M) {
         const unsigned b = d.mbit[m];
-        d.mhist[m] = (d.mhist[m] << 1) | ((d.recv[b >> 5] >> (b & 31)) & 1u);
+        const unsigned spk = (d.recv[b >> 5] >> (b & 31)) & 1u;
+        d.mhist[m] = (d.mhist[m] << 1) | spk;
+        if (spk)  // the pre's mirror groups are [mbeg[m], mbeg[m + 1]) (group indices)
+            for (int g = d.mbeg[m]; g < d.mbeg[m + 1]; ++g) {
+                const unsigned meta = d.gmeta[g];
+                float2 v = d.gview[g];
+                const unsigned add = GV_DISP | GV_EV | ((meta & GV_D_MASK) == 1u ? GV_NEXT : 0u);
+                v.y = __uint_as_float(__float_as_uint(v.y) | add);
+                d.gview[g] = v;
+                disp_cnt += gw_size(meta);
+            }
     }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) disp_cnt += __shfl_xor_sync(0xffffffffu, disp_cnt, o);
+    if ((threadIdx.x & 31) == 0 && disp_cnt) atomicAdd(&d.ctrl->dispatched, disp_cnt);
 }
 
 __global__ void __launch_bounds__(256) k_mirror_groups(Dev d, Consts k) {
-    const long long t = d.ctrl->t;
+    // step t = next_t: k_neurons of the same step may be running, and it
+    // publishes ctrl->t only for the synapse pass
+    const long long t = d.ctrl->next_t;
     const long long x = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     unsigned long long arr_cnt = 0, disp_cnt = 0;
     if (x < d.GM) {
         const int g = (int)(d.G_local + x);
-        update_group(d, k, g, d.gmeta[g], d.gstate[g], d.gextra[g], d.mhist[d.gmir[x]], t, arr_cnt,
+        update_group(d, k, g, d.gmeta[g], d.gstate[g], d.gextra[g], d.mhist[d.gmir[x]] << 1, t, arr_cnt,
                      disp_cnt);
     }
 #pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) {
-        arr_cnt += __shfl_xor_sync(0xffffffffu, arr_cnt, o);
-        disp_cnt += __shfl_xor_sync(0xffffffffu, disp_cnt, o);
-    }
-    if ((threadIdx.x & 31) == 0) {
-        if (arr_cnt) {
-            atomicAdd(&d.ctrl->arrivals, arr_cnt);
-            atomicAdd(&d.ctrl->step_arrivals[t & 1], arr_cnt);
-        }
-        if (disp_cnt) atomicAdd(&d.ctrl->dispatched, disp_cnt);
+    for (int o = 16; o >= 1; o >>= 1) arr_cnt += __shfl_xor_sync(0xffffffffu, arr_cnt, o);
+    if ((threadIdx.x & 31) == 0 && arr_cnt) {
+        atomicAdd(&d.ctrl->arrivals, arr_cnt);
+        atomicAdd(&d.ctrl->step_arrivals[t & 1], arr_cnt);
     }
 }
 
@@ -1065,6 +1084,10 @@ struct Engine2e : snnb::Engine {
     // payload buffers and the mirror groups of remote pres
     int rank = 0, world = 1;
     ncclComm_t comm = nullptr;
+    // sharded runs: the mirror-group update runs on a side stream, forked at
+    // the start of each step and joined before the exchange's fix-up
+    cudaStream_t side = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
     Shard sh;
     std::vector<int64_t> new_of_old;  // layout group id -> device group id
     snnb::DevBuf<unsigned> send, recv, mbit, mhist;
@@ -1079,13 +1102,19 @@ struct Engine2e : snnb::Engine {
     }
     ~Engine2e() override {
         for (auto e : pev) cudaEventDestroy(e);
+        if (ev_fork) cudaEventDestroy(ev_fork);
+        if (ev_join) cudaEventDestroy(ev_join);
         for (auto e : run_ev)
             if (e) cudaEventDestroy(e);
         // graphs holding NCCL calls go before the communicator
         if (graph_exec) cudaGraphExecDestroy(graph_exec);
         if (graph) cudaGraphDestroy(graph);
         if (stream) cudaStreamSynchronize(stream);
-        if (comm) ncclCommDestroy(comm);
+        if (comm) snnb::nccl().CommDestroy(comm);
+        if (side) {
+            cudaStreamSynchronize(side);
+            cudaStreamDestroy(side);
+        }
         if (stream) {
             cudaStreamDestroy(stream);
         }
@@ -1153,6 +1182,7 @@ struct Engine2e : snnb::Engine {
     void set_shard(int32_t r, int32_t w, const void* uid) override {
         SNN_REQUIRE(!built, SNN_ERR_STATE, "shard before building the network");
         SNN_REQUIRE(w >= 1 && r >= 0 && r < w, SNN_ERR_ARG, "bad rank / world size");
+        SNN_REQUIRE(comm == nullptr, SNN_ERR_STATE, "the network is sharded already");
         rank = r;
         world = w;
         if (w > 1) {
@@ -1160,9 +1190,13 @@ struct Engine2e : snnb::Engine {
             ncclUniqueId id;
             memcpy(&id, uid, sizeof(id));
             SNN_CUDA(cudaSetDevice(cfg.device));
-            ncclResult_t nr = ncclCommInitRank(&comm, w, id, r);
+            const snnb::NcclApi& nc = snnb::nccl();
+            ncclResult_t nr = nc.CommInitRank(&comm, w, id, r);
             SNN_REQUIRE(nr == ncclSuccess, SNN_ERR_CUDA,
-                        std::string("ncclCommInitRank: ") + ncclGetErrorString(nr));
+                        std::string("ncclCommInitRank: ") + nc.GetErrorString(nr));
+            SNN_CUDA(cudaStreamCreateWithFlags(&side, cudaStreamNonBlocking));
+            SNN_CUDA(cudaEventCreateWithFlags(&ev_fork, cudaEventDisableTiming));
+            SNN_CUDA(cudaEventCreateWithFlags(&ev_join, cudaEventDisableTiming));
         }
     }
 
@@ -1409,13 +1443,20 @@ struct Engine2e : snnb::Engine {
         const unsigned fl = capturing ? cudaEventRecordExternal : cudaEventRecordDefault;
         int e = 0;
         if (ev) SNN_CUDA(cudaEventRecordWithFlags(ev[e++], st, fl));
+        if (world > 1) {  // mirror groups from spikes up to t - 1, beside k_neurons and the exchange
+            SNN_CUDA(cudaEventRecord(ev_fork, st));
+            SNN_CUDA(cudaStreamWaitEvent(side, ev_fork, 0));
+            k_mirror_groups<<<(unsigned)std::max(1ll, (D.GM + 255) / 256), 256, 0, side>>>(D, K);
+            SNN_CUDA(cudaEventRecord(ev_join, side));
+        }
         k_neurons<<<nb, NEU_BLOCK, 0, st>>>(D, K);
         if (ev) SNN_CUDA(cudaEventRecordWithFlags(ev[e++], st, fl));
         if (world > 1) {
-            const ncclResult_t nr = ncclAllGather(send.p, recv.p, (size_t)D.pw, ncclUint32, comm, st);
-            SNN_REQUIRE(nr == ncclSuccess, SNN_ERR_CUDA, std::string("ncclAllGather: ") + ncclGetErrorString(nr));
+            const snnb::NcclApi& nc = snnb::nccl();
+            const ncclResult_t nr = nc.AllGather(send.p, recv.p, (size_t)D.pw, ncclUint32, comm, st);
+            SNN_REQUIRE(nr == ncclSuccess, SNN_ERR_CUDA, std::string("ncclAllGather: ") + nc.GetErrorString(nr));
+            SNN_CUDA(cudaStreamWaitEvent(st, ev_join, 0));
             k_mirror_hist<<<std::max(1, (D.M + 255) / 256), 256, 0, st>>>(D);
-            k_mirror_groups<<<(unsigned)std::max(1ll, (D.GM + 255) / 256), 256, 0, st>>>(D, K);
             if (ev) SNN_CUDA(cudaEventRecordWithFlags(ev[e++], st, fl));
         }
         k_synapses<<<syn_grid, SYN_THREADS, syn_smem, st>>>(D, K);

@@ -81,5 +81,7 @@ def test_two_rank_column_shards_match_the_oracle(tmp_path):
             c = json.load(fh)
         assert c["total_spikes"] == total  # global on every rank
     oc = orc.counters()
-    arrivals = sum(json.load(open(tmp_path / f"counters{r}.json"))["arrivals"] for r in range(2))
-    assert arrivals == oc.arrived
+    cs = [json.load(open(tmp_path / f"counters{r}.json")) for r in range(2)]
+    assert sum(c["arrivals"] for c in cs) == oc.arrived
+    # every (pre spike, synapse) dispatch is counted once, on the rank of the synapse's post
+    assert sum(c["dispatched"] for c in cs) == oc.dispatched
