@@ -81,3 +81,20 @@ def test_stream_presets_byte_classes():
     b.tobytes()[:-3].decode("utf-8", errors="strict")
     assert np.array_equal(snn.stream(1000, seed=5), snn.stream(1000, seed=5))
     assert not np.array_equal(snn.stream(1000, seed=5), snn.stream(1000, seed=6))
+
+
+def test_library_does_not_link_nccl_and_torch_loads_after_it():
+    """NCCL is opened at run time by sharded runs only: the library has no
+    link-time libnccl dependency, so importing torch after loading it keeps
+    torch's own NCCL build (a system libnccl loaded first would take the
+    soname and leave torch's newer NCCL symbols unresolved)."""
+    import subprocess
+    import sys
+    out = subprocess.run(["readelf", "-d", snn.LIB_PATH], capture_output=True, text=True)
+    assert out.returncode == 0, out.stderr
+    needed = [ln for ln in out.stdout.splitlines() if "(NEEDED)" in ln]
+    assert needed and not any("nccl" in ln for ln in needed), needed
+    code = ("import sys; sys.path.insert(0, %r); import snn_b200 as snn; snn.lib(); "
+            "import torch; print('ok', torch.__version__)" % os.path.dirname(snn.LIB_PATH))
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and r.stdout.startswith("ok"), r.stderr[-2000:]
