@@ -8,7 +8,11 @@
 //            loads, one int32 red.add per synapse into the L2-resident
 //            accumulator (exact, so order-free); LTD fused on the same
 //            registers (w rewritten with 16-byte streaming stores).
-//   k4_lif   thread per neuron: LIF on the accumulator (zeroing it), raster
+//   k4_push_b (bucketed form, chosen at higher rates) CTA per (post bucket,
+//            part of the spikers): shared-memory accumulation of the CTA's
+//            row segments, stored to its row of per-part sums
+//   k4_lif   thread per neuron: LIF on the accumulator (zeroing it) or on the
+//            sum of the per-part rows of the bucketed push, raster
 //            word by ballot, list of LIF spikes (STDP), and the forced spikes
 //            of step t+1 with their Tsodyks-Markram release (warp-aggregated
 //            appends to the double-buffered pre-spike list; step t+1's push
@@ -62,7 +66,9 @@ struct PDev {
     const float* exp_tab;
     PCtrl* ctrl;
     const uint16_t* boff;     // [N][nb + 1] start of each post bucket in the (sorted) row
-    int nb, bshift, parts;    // buckets of 2^bshift posts; CTAs per bucket in k4_push_b
+    int nb, bw, parts;        // nb buckets of bw posts; CTAs per bucket in k4_push_b
+    int32_t* part;            // [parts][N] sums of the bucketed push, one writer per slot
+    int lif_parts;            // > 0: k4_lif sums part[0 .. lif_parts) instead of acc
 };
 
 __device__ __forceinline__ float e20(const PDev& D, int dt) {
@@ -233,27 +239,36 @@ __global__ void __launch_bounds__(P_THREADS) k4_push_scalar(PDev D, int k) {
     }
 }
 
-// Bucketed push: CTA (b, p) owns the posts [b << bshift, (b + 1) << bshift)
+// Bucketed push: CTA (b, p) owns the posts [b bw, (b + 1) bw)
 // and spikers [n p / parts, n (p + 1) / parts).  Each row's synapses are
 // stored grouped by post bucket (boff gives the segment of bucket b), so the
 // CTA reads only its segments and accumulates them with shared-memory
-// atomics; at the end it adds its non-zero slots to the global accumulator
-// (at most one L2 atomic per slot instead of one per synapse).  A group of
-// B_G lanes streams B_SP spikers' segments at once (B_U loads deep each, the
-// segments average fan-out / buckets synapses); the spiker ids and segment
-// bounds of the group's next spikers are fetched while these stream.
+// atomics; at the end it stores its slots to its own row of part[parts][N]
+// (coalesced plain stores: every slot has one writer), which k4_lif sums.  A group of
+// B_G lanes streams B_SP spikers' segments at once, B_U loads deep each, so
+// that a segment (fan-out / buckets synapses on average, ~48 at 1M x 1,000
+// in 21 buckets) is usually read in one round trip; the spiker ids and
+// segment bounds of the group's next spikers are fetched while these stream.
+// Measured at 1M x 1,000 (10 % forced rate): B_G 8, B_U 8, B_SP 1 streams the
+// push in 194 us, against 269 us for 16 x 4 x 1 and 434 us for 8 x 4 x 2.
 #ifndef SNN_B_THREADS
 #define SNN_B_THREADS 1024
 #endif
 #ifndef SNN_B_SP
-#define SNN_B_SP 2
+#define SNN_B_SP 1
 #endif
-#ifndef SNN_B_SHIFT
-#define SNN_B_SHIFT 15
+#ifndef SNN_B_WMAX
+#define SNN_B_WMAX 58112  // widest bucket (int32 slots of shared memory per CTA)
+#endif
+#ifndef SNN_B_G
+#define SNN_B_G 8
+#endif
+#ifndef SNN_B_U
+#define SNN_B_U 8
 #endif
 constexpr int B_THREADS = SNN_B_THREADS;
-constexpr int B_G = 8;
-constexpr int B_U = 4;
+constexpr int B_G = SNN_B_G;
+constexpr int B_U = SNN_B_U;
 constexpr int B_SP = SNN_B_SP;
 
 template <bool STDP, bool STP>
@@ -293,8 +308,8 @@ __global__ void __launch_bounds__(B_THREADS) k4_push_b(PDev D, int k) {
         C->pre_spikes += n;
     }
     const int b = blockIdx.x % D.nb, p = blockIdx.x / D.nb;
-    const int lo_post = b << D.bshift;
-    const int width = min(1 << D.bshift, D.N - lo_post);
+    const int lo_post = b * D.bw;
+    const int width = min(D.bw, D.N - lo_post);
     for (int x = threadIdx.x; x < width; x += B_THREADS) acc_s[x] = 0;
     __syncthreads();
     const long long e_lo = (long long)n * p / D.parts, e_hi = (long long)n * (p + 1) / D.parts;
@@ -377,10 +392,8 @@ __global__ void __launch_bounds__(B_THREADS) k4_push_b(PDev D, int k) {
                 push_b_chunk<STDP, STP>(D, j0, o1[sp], base[sp], lo_post, acc_s, rel[sp], plastic[sp], t, lr);
     }
     __syncthreads();
-    for (int x = threadIdx.x; x < width; x += B_THREADS) {
-        const int v = acc_s[x];
-        if (v) atomicAdd(D.acc + lo_post + x, v);
-    }
+    int32_t* out = D.part + (size_t)p * D.N + lo_post;
+    for (int x = threadIdx.x; x < width; x += B_THREADS) out[x] = acc_s[x];
 }
 
 template <bool STDP, bool STP>
@@ -391,8 +404,16 @@ __global__ void __launch_bounds__(P_THREADS) k4_lif(PDev D, int k) {
     const int lane = threadIdx.x & 31;
     bool sp = false;
     if (j < D.N) {
-        const int a = __ldcg(D.acc + j);
-        D.acc[j] = 0;
+        // this step's input: the accumulator of the direct push (consumed
+        // and cleared), or the per-part sums of the bucketed push (int32
+        // addition: the same value in any order)
+        int a = 0;
+        if (D.lif_parts == 0) {
+            a = __ldcg(D.acc + j);
+            D.acc[j] = 0;
+        } else {
+            for (int q = 0; q < D.lif_parts; ++q) a += __ldcg(D.part + (size_t)q * D.N + j);
+        }
         const float in = pm_mul(pm_i2f(a), Q_SCALE_INV);
         const int r = D.ref[j];
         float v = D.V[j];
@@ -490,13 +511,13 @@ __global__ void k4_generate(int32_t* post, float* w, long long S, int N, int F, 
     }
 }
 
-// Row i's synapses grouped by post bucket (post >> bshift), stable in k:
+// Row i's synapses grouped by post bucket (post / bw), stable in k:
 // one warp per row; writes the sorted post / w and the bucket starts.  With
 // `unpermute` set it instead scatters a sorted per-synapse array back to the
 // generation order (s = i * F + k): out[i F + k] = in[i F + pos(k)].
 __global__ void __launch_bounds__(256) k4_sort_rows(int32_t* post, float* w, uint16_t* boff, int N, int F,
                                                     int n_exc, uint32_t seed, float w_max, int nb,
-                                                    int bshift, const uint32_t* in, uint32_t* out) {
+                                                    int bw, const uint32_t* in, uint32_t* out) {
     extern __shared__ int sm[];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     int* cnt = sm + wib * 2 * (nb + 1);
@@ -509,7 +530,7 @@ __global__ void __launch_bounds__(256) k4_sort_rows(int32_t* post, float* w, uin
         __syncwarp();
         for (int kk = lane; kk < F; kk += 32) {
             const int q = snn_prop_post(snn_prop_syn_hash(seed, (uint64_t)(row + kk)), (uint32_t)N);
-            atomicAdd(cnt + (q >> bshift), 1);
+            atomicAdd(cnt + q / bw, 1);
         }
         __syncwarp();
         if (lane == 0) {
@@ -529,7 +550,7 @@ __global__ void __launch_bounds__(256) k4_sort_rows(int32_t* post, float* w, uin
             if (valid) {
                 h = snn_prop_syn_hash(seed, (uint64_t)(row + kk));
                 q = snn_prop_post(h, (uint32_t)N);
-                bk = q >> bshift;
+                bk = q / bw;
             }
             const unsigned peers = __match_any_sync(0xffffffffu, bk);
             const int rank = __popc(peers & ((1u << lane) - 1u));
@@ -611,7 +632,7 @@ struct EngineProp : snnb::Engine {
     int push_grid = 1, lif_grid = 1, ltp_grid = 1;
     uint32_t max_in = 0, spec_seed = 0;
     float dopamine = 1.0f;
-    snnb::DevBuf<int32_t> post, acc, last_post, tA, tB, pre_list, post_list;
+    snnb::DevBuf<int32_t> post, acc, last_post, tA, tB, pre_list, post_list, part;
     snnb::DevBuf<float> w, V, I, u, R, rel_list, un_list, rn_list, exp_tab;
     snnb::DevBuf<int8_t> ref;
     snnb::DevBuf<uint32_t> in_ptr, rev, raster, tmp;
@@ -673,30 +694,60 @@ struct EngineProp : snnb::Engine {
                   : (cfg.prop_rate > 0.0f ? pm_div(0.01f, pm_mul(cfg.prop_rate, (float)F)) : 1.0f);
         SNN_REQUIRE(D.w_max <= 1.0f, SNN_ERR_ARG, "prop_w_max must be <= 1");
         vec = (F % 4) == 0;
-        // rows grouped by post bucket of 2^bshift posts (2^bshift int32 slots)
-        D.bshift = SNN_B_SHIFT;
-        D.nb = (int)(((long long)N + (1 << D.bshift) - 1) >> D.bshift);
-        sorted = D.nb <= 256 && F <= 65535;
+        // rows grouped by post bucket of bw posts (bw int32 slots of shared
+        // memory per CTA of k4_push_b): among the bucket counts whose buckets
+        // fit (bw <= SNN_B_WMAX and the opt-in shared memory), the fewest
+        // (widest buckets, longest row segments) whose nb x parts CTAs fill
+        // the SMs in whole waves within 1 % of the best fill
+        int dev_sms = 0, smem_optin = 0;
+        SNN_CUDA(cudaDeviceGetAttribute(&dev_sms, cudaDevAttrMultiProcessorCount, cfg.device));
+        SNN_CUDA(cudaDeviceGetAttribute(&smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, cfg.device));
+        const int bw_cap = std::max(1024, std::min(SNN_B_WMAX, smem_optin / 4));
+        const int nb_min = (int)(((long long)N + bw_cap - 1) / bw_cap);
+        sorted = nb_min <= 256 && F <= 65535;
         SNN_REQUIRE(cfg.prop_push >= 0 && cfg.prop_push <= 2, SNN_ERR_ARG, "prop_push must be 0, 1 or 2");
         SNN_REQUIRE(cfg.prop_push != 2 || sorted, SNN_ERR_ARG,
-                    "bucketed push needs at most 256 buckets of 32768 posts and fan-out <= 65535");
-        int dev_sms = 0;
-        SNN_CUDA(cudaDeviceGetAttribute(&dev_sms, cudaDevAttrMultiProcessorCount, cfg.device));
-        push_smem = (size_t)4 << D.bshift;
-        int bocc = 0;
+                    "bucketed push needs at most 256 post buckets and fan-out <= 65535");
+        D.nb = nb_min;
+        D.bw = (int)(((long long)N + nb_min - 1) / nb_min);
+        D.parts = 1;
         if (sorted) {
             for (auto kf : {k4_push_b<false, false>, k4_push_b<false, true>, k4_push_b<true, false>,
                             k4_push_b<true, true>})
-                SNN_CUDA(cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)push_smem));
-            SNN_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bocc, push_kernel_b(), B_THREADS, push_smem));
-            // whole waves only: a partial second wave would double the step
-            D.parts = std::max(1, (std::max(bocc, 1) * dev_sms) / D.nb);
+                SNN_CUDA(cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_optin));
+            struct Cand { int nb, bw, parts; double util; };
+            std::vector<Cand> cands;
+            double best = 0.0;
+            for (int nb = nb_min; nb <= std::min(256, std::max(2 * nb_min, nb_min + 8)); ++nb) {
+                const int bw = (int)(((long long)N + nb - 1) / nb);
+                if ((int)(((long long)N + bw - 1) / bw) != nb) continue;  // nb buckets of bw cover N
+                int occ = 0;
+                SNN_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, push_kernel_b(), B_THREADS,
+                                                                       (size_t)4 * bw));
+                if (occ < 1) continue;
+                const int slots = occ * dev_sms;
+                const int parts = std::max(1, slots / nb);
+                const long long ctas = (long long)nb * parts;
+                const double util = (double)ctas / (double)(((ctas + slots - 1) / slots) * slots);
+                cands.push_back({nb, bw, parts, util});
+                best = std::max(best, util);
+            }
+            SNN_REQUIRE(!cands.empty(), SNN_ERR_CUDA, "no bucket width fits the bucketed push");
+            for (const Cand& c : cands)
+                if (c.util >= best - 0.01) {
+                    D.nb = c.nb;
+                    D.bw = c.bw;
+                    D.parts = c.parts;
+                    break;
+                }
         }
-        // bucketed when the expected events per step reach 2 * parts per post
-        // (the flush then costs well under one L2 atomic per synapse it
-        // replaces; measured break-even near 1 % at 1M x 1,000)
+        push_smem = (size_t)4 * D.bw;
+        // bucketed when a post expects at least one event per step (measured
+        // at 1M x 1,000: the bucketed step is faster from 0.1 % forced rate
+        // up, 1.4x at 1 %, 2.7x at 10 %; the direct push only wins, by ~1 %,
+        // at 0.1 % with STDP)
         bucketed = cfg.prop_push == 2 ||
-                   (cfg.prop_push == 0 && sorted && (double)cfg.prop_rate * F >= 2.0 * D.parts);
+                   (cfg.prop_push == 0 && sorted && (double)cfg.prop_rate * F >= 1.0);
 
         post.alloc(S);
         w.alloc(S);
@@ -717,7 +768,7 @@ struct EngineProp : snnb::Engine {
         if (sorted) {
             boff.alloc((size_t)N * (D.nb + 1));
             k4_sort_rows<<<gen_grid, 256, 8 * 2 * (D.nb + 1) * sizeof(int), stream>>>(
-                post.p, w.p, boff.p, N, F, D.n_exc, spec.seed, D.w_max, D.nb, D.bshift, nullptr, nullptr);
+                post.p, w.p, boff.p, N, F, D.n_exc, spec.seed, D.w_max, D.nb, D.bw, nullptr, nullptr);
         } else {
             k4_generate<<<gen_grid, 256, 0, stream>>>(post.p, w.p, S, N, F, D.n_exc, spec.seed, D.w_max);
         }
@@ -756,6 +807,12 @@ struct EngineProp : snnb::Engine {
         D.un_list = un_list.p; D.rn_list = rn_list.p;
         D.post_list = post_list.p; D.raster = raster.p; D.exp_tab = exp_tab.p; D.ctrl = ctrl.p;
         D.boff = boff.p;
+        if (bucketed) {
+            part.alloc((size_t)D.parts * N);
+            part.zero(stream);
+        }
+        D.part = part.p;
+        D.lif_parts = bucketed ? D.parts : 0;
         reset_state();
         int occ = 0;
         if (vec) SNN_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, push_kernel(), P_THREADS, 0));
@@ -1021,7 +1078,7 @@ struct EngineProp : snnb::Engine {
         if (sorted) {
             tmpo.alloc(S);
             k4_sort_rows<<<148 * 16, 256, 8 * 2 * (D.nb + 1) * sizeof(int), stream>>>(
-                nullptr, nullptr, nullptr, D.N, D.F, D.n_exc, spec_seed, D.w_max, D.nb, D.bshift,
+                nullptr, nullptr, nullptr, D.N, D.F, D.n_exc, spec_seed, D.w_max, D.nb, D.bw,
                 (const uint32_t*)src, tmpo.p);
             SNN_CUDA(cudaGetLastError());
             from = tmpo.p;
@@ -1043,12 +1100,13 @@ struct EngineProp : snnb::Engine {
         int64_t steps, raster_base, N, S;
         float dopamine, w_max;
         int32_t mode, raster_cap;
-        uint32_t thr, pad;
+        uint32_t thr, bw;  // bw: bucket width of the stored row order (0: generation order)
     };
     NativeBlob blob() const {
         NativeBlob b{};
         b.steps = steps; b.raster_base = raster_base_host; b.N = D.N; b.S = S;
         b.dopamine = dopamine; b.w_max = D.w_max; b.mode = mode; b.raster_cap = raster_cap; b.thr = D.thr;
+        b.bw = sorted ? (uint32_t)D.bw : 0u;
         return b;
     }
     std::vector<snnb::DevSection> native_sections() {
@@ -1079,7 +1137,7 @@ struct EngineProp : snnb::Engine {
                               memcpy(&f, p, sizeof(f));
                               SNN_REQUIRE(f.N == want.N && f.S == want.S && f.mode == want.mode &&
                                               f.thr == want.thr && f.raster_cap == want.raster_cap &&
-                                              f.w_max == want.w_max,
+                                              f.w_max == want.w_max && f.bw == want.bw,
                                           SNN_ERR_IO, "checkpoint of another microbench network");
                           });
         steps = got.steps;
