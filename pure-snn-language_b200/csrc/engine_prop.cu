@@ -75,12 +75,16 @@ __device__ __forceinline__ float e20(const PDev& D, int dt) {
     return dt <= SNN_PROP_EXP_STEPS ? __ldg(D.exp_tab + dt) : 0.0f;
 }
 
-// LTD of one excitatory out-synapse onto q (post spike strictly before t)
-__device__ __forceinline__ float ltd(const PDev& D, float w, int q, int t, float lr) {
-    const int lp = __ldcg(D.last_post + q);
+// LTD of one excitatory out-synapse whose post last spiked at lp (strictly
+// before t; lp < 0: never)
+__device__ __forceinline__ float ltd_lp(const PDev& D, float w, int lp, int t, float lr) {
     if (lp < 0) return w;
     const float dw = pm_mul(-0.05f, e20(D, t - lp));
     return pm_min(pm_max(pm_fma(lr, dw, w), 0.0f), D.w_max);
+}
+// the same, onto post q
+__device__ __forceinline__ float ltd(const PDev& D, float w, int q, int t, float lr) {
+    return ltd_lp(D, w, __ldcg(D.last_post + q), t, lr);
 }
 
 // warp-aggregated append of flagged lanes to list[] (count at *cnt)
@@ -273,7 +277,8 @@ constexpr int B_SP = SNN_B_SP;
 
 template <bool STDP, bool STP>
 __device__ __forceinline__ void push_b_chunk(const PDev& D, int j0, int o1, long long base, int lo_post,
-                                             int* acc_s, float rel, bool plastic, int t, float lr) {
+                                             int* acc_s, const int* lp_s, float rel, bool plastic, int t,
+                                             float lr) {
     int q[B_U];
     float wv[B_U];
 #pragma unroll
@@ -289,7 +294,7 @@ __device__ __forceinline__ void push_b_chunk(const PDev& D, int j0, int o1, long
         const int j = j0 + u * B_G;
         if (j < o1) {
             atomicAdd(acc_s + (q[u] - lo_post), snn_prop_quant(wv[u], rel, STP));
-            if (plastic) D.w[base + j] = ltd(D, wv[u], q[u], t, lr);
+            if (plastic) D.w[base + j] = ltd_lp(D, wv[u], lp_s[q[u] - lo_post], t, lr);
         }
     }
 }
@@ -310,7 +315,14 @@ __global__ void __launch_bounds__(B_THREADS) k4_push_b(PDev D, int k) {
     const int b = blockIdx.x % D.nb, p = blockIdx.x / D.nb;
     const int lo_post = b * D.bw;
     const int width = min(D.bw, D.N - lo_post);
-    for (int x = threadIdx.x; x < width; x += B_THREADS) acc_s[x] = 0;
+    // with STDP the bucket's last post spikes follow the slots in shared
+    // memory, so that the fused LTD reads them there
+    int* const lp_s = acc_s + D.bw;
+    const bool learn_s = STDP && C->learn;
+    for (int x = threadIdx.x; x < width; x += B_THREADS) {
+        acc_s[x] = 0;
+        if (learn_s) lp_s[x] = __ldcg(D.last_post + lo_post + x);
+    }
     __syncthreads();
     const long long e_lo = (long long)n * p / D.parts, e_hi = (long long)n * (p + 1) / D.parts;
     const int gl = threadIdx.x & (B_G - 1);
@@ -382,14 +394,15 @@ __global__ void __launch_bounds__(B_THREADS) k4_push_b(PDev D, int k) {
                 const int j = o0[sp] + gl + u * B_G;
                 if (j < o1[sp]) {
                     atomicAdd(acc_s + (q[sp][u] - lo_post), snn_prop_quant(wv[sp][u], rel[sp], STP));
-                    if (plastic[sp]) D.w[base[sp] + j] = ltd(D, wv[sp][u], q[sp][u], t, lr);
+                    if (plastic[sp]) D.w[base[sp] + j] = ltd_lp(D, wv[sp][u], lp_s[q[sp][u] - lo_post], t, lr);
                 }
             }
         // rare long segments
 #pragma unroll
         for (int sp = 0; sp < B_SP; ++sp)
             for (int j0 = o0[sp] + B_G * B_U + gl; j0 < o1[sp]; j0 += B_G * B_U)
-                push_b_chunk<STDP, STP>(D, j0, o1[sp], base[sp], lo_post, acc_s, rel[sp], plastic[sp], t, lr);
+                push_b_chunk<STDP, STP>(D, j0, o1[sp], base[sp], lo_post, acc_s, lp_s, rel[sp], plastic[sp], t,
+                                        lr);
     }
     __syncthreads();
     int32_t* out = D.part + (size_t)p * D.N + lo_post;
@@ -702,7 +715,8 @@ struct EngineProp : snnb::Engine {
         int dev_sms = 0, smem_optin = 0;
         SNN_CUDA(cudaDeviceGetAttribute(&dev_sms, cudaDevAttrMultiProcessorCount, cfg.device));
         SNN_CUDA(cudaDeviceGetAttribute(&smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, cfg.device));
-        const int bw_cap = std::max(1024, std::min(SNN_B_WMAX, smem_optin / 4));
+        const int slot_bytes = stdp ? 8 : 4;  // int32 sum (+ int32 last post spike with STDP)
+        const int bw_cap = std::max(1024, std::min(SNN_B_WMAX, smem_optin / slot_bytes));
         const int nb_min = (int)(((long long)N + bw_cap - 1) / bw_cap);
         sorted = nb_min <= 256 && F <= 65535;
         SNN_REQUIRE(cfg.prop_push >= 0 && cfg.prop_push <= 2, SNN_ERR_ARG, "prop_push must be 0, 1 or 2");
@@ -723,7 +737,7 @@ struct EngineProp : snnb::Engine {
                 if ((int)(((long long)N + bw - 1) / bw) != nb) continue;  // nb buckets of bw cover N
                 int occ = 0;
                 SNN_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, push_kernel_b(), B_THREADS,
-                                                                       (size_t)4 * bw));
+                                                                       (size_t)slot_bytes * bw));
                 if (occ < 1) continue;
                 const int slots = occ * dev_sms;
                 const int parts = std::max(1, slots / nb);
@@ -741,7 +755,7 @@ struct EngineProp : snnb::Engine {
                     break;
                 }
         }
-        push_smem = (size_t)4 * D.bw;
+        push_smem = (size_t)slot_bytes * D.bw;
         // bucketed when a post expects at least one event per step (measured
         // at 1M x 1,000: the bucketed step is faster from 0.1 % forced rate
         // up, 1.4x at 1 %, 2.7x at 10 %; the direct push only wins, by ~1 %,
