@@ -203,12 +203,23 @@ def prop_cpu_baseline(rate, budget_s=10.0):
 
 
 def prop_main(args):
-    """Propagation microbench: one JSON line per (mode, rate)."""
+    """Propagation microbench: one JSON line per (mode, rate).  Under torchrun
+    the network is sharded by post bucket over the ranks (one GPU each; the
+    forced pre-spikes are drawn on every rank, so nothing is exchanged during
+    the run): strong scaling, device time max over ranks, events summed."""
+    import datetime
     import snn_b200 as snn
     import torch
+    import torch.distributed as tdist
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        tdist.init_process_group("gloo", timeout=datetime.timedelta(seconds=900))
+    torch.cuda.set_device(local)
     warm = max(args.warmup, 3)
     peak, peak_kind = measured_peaks()
-    cb = None if args.no_cpu_baseline else prop_cpu_baseline(0.01)
+    cb = None if args.no_cpu_baseline or world > 1 else prop_cpu_baseline(0.01)
     rates = [float(x) for x in args.prop_rates.split(",")] if args.prop_rates else PROP_RATES
     modes = [m for m in PROP_MODES if not args.prop_modes or str(m[0]) in args.prop_modes.split(",")]
     n_neu = args.prop_neurons
@@ -216,14 +227,18 @@ def prop_main(args):
     traffic_per_event = profile_traffic("k4_push_b_propagation_1M.md", "traffic_bytes_per_event")
     for mode, mname in modes:
         for rate in rates:
-            net = snn.Network(model=snn.MODEL_PROP, prop_mode=mode, prop_rate=rate)
+            net = snn.Network(device=local, model=snn.MODEL_PROP, prop_mode=mode, prop_rate=rate)
+            if world > 1:
+                net.set_shard(rank, world)
             net.build_columns(snn.topology(snn.MODEL_PROP, l4=n_neu))
             net.run(warm)
             net.synchronize()
             c0 = net.counters()
             torch.cuda.synchronize()
             net.set_profiling(True)
-            with ClockSampler(0) as clk:
+            if world > 1:
+                tdist.barrier()
+            with ClockSampler(local) as clk:
                 net.run(args.steps)
                 net.synchronize()
             prof = net.profile()
@@ -241,24 +256,42 @@ def prop_main(args):
             raster = torch.empty((args.steps, net.words), dtype=torch.int32, pin_memory=True)
             ce0 = net.counters()
             torch.cuda.synchronize()
+            if world > 1:
+                tdist.barrier()
             t0 = time.perf_counter()
             net._check(net.L.snn_run(net.h, args.steps, None, 0, 1, raster.data_ptr(), None))
             net.synchronize()
             wall = time.perf_counter() - t0
             e2e_ev = net.counters()["arrivals"] - ce0["arrivals"]
+            post_sp = c1["total_spikes"] - c0["total_spikes"]
+            ltp_v = c1["ltp_visits"] - c0["ltp_visits"]
+            if world > 1:  # device time and wall time: max over ranks; events: sum
+                tv = torch.tensor([dev_s, wall, push_s], dtype=torch.float64)
+                te = torch.tensor([ev, e2e_ev, post_sp, ltp_v], dtype=torch.float64)
+                tdist.all_reduce(tv, op=tdist.ReduceOp.MAX)
+                tdist.all_reduce(te, op=tdist.ReduceOp.SUM)
+                dev_s, wall, push_s = (float(x) for x in tv)
+                ev, e2e_ev, post_sp, ltp_v = (float(x) for x in te)
+                pb = prop_push_bytes(ev, pre * world, mode) / args.steps / world  # per rank
+                achieved = pb / push_s / 1e9
+            if rank != 0:
+                net.close()
+                continue
             line = {
                 "metric": f"synaptic events/sec (SOPS), propagation microbench {n_neu:,} x 1,000",
-                "value": ev / dev_s, "unit": UNIT, "n_gpus": 1, "steps": args.steps,
-                "warmup": warm, "ms_per_step": prof["step_ms"] / args.steps,
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "value": ev / dev_s, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": warm, "ms_per_step": dev_s * 1000.0 / args.steps,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
                 "dtype": "f32 weights, int32 fixed-point sums",
                 "data": "synthetic (seeded forced Poisson pre-spikes)",
                 "config": {"workload": f"propagation microbench, {n_neu:,} LIF x fan-out 1,000 "
                                        f"({n_neu * 1000 / 1e9:.1f}B synapses), rate {rate}, {mname}",
                            "rate": rate, "mode": mname,
                            "events_per_step": ev / args.steps,
-                           "post_spikes_per_step": (c1["total_spikes"] - c0["total_spikes"]) / args.steps,
-                           "ltp_visits_per_step": (c1["ltp_visits"] - c0["ltp_visits"]) / args.steps,
+                           "post_spikes_per_step": post_sp / args.steps,
+                           "ltp_visits_per_step": ltp_v / args.steps,
+                           "parallelism": f"post-bucket shards x{world}" if world > 1 else "1 GPU",
+                           "exchange": "none during the run (forced pre-spikes drawn on every rank)",
                            "l2": "inputs larger than L2 (8 GB of synapse streams)"},
                 "e2e": {"value": e2e_ev / wall, "unit": UNIT, "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": net.words * 4},
@@ -268,7 +301,7 @@ def prop_main(args):
                 "roofline": {"bound": "hbm", "kernel": pname, "achieved": achieved,
                              "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                              "peak_kind": peak_kind, "bytes_per_launch": pb,
-                             "traffic": traffic_per_event * ev / args.steps
+                             "traffic": traffic_per_event * ev / args.steps / world
                              if pname == "k4_push_b" and mode == 0 and traffic_per_event else None},
                 "clocks": clk.summary(),
             }
@@ -276,6 +309,9 @@ def prop_main(args):
                 line["cpu_baseline"] = cb
             print(json.dumps(line), flush=True)
             net.close()
+    if world > 1:
+        tdist.barrier()
+        tdist.destroy_process_group()
 
 
 def stage0_main(args):
@@ -452,7 +488,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="stage2e", choices=["stage2e", "prop", "shard", "stage0"],
                     help="stage2e: the 55k/10.7M network (one line); prop: the 1M x 1,000 "
-                         "propagation microbench (one line per mode and rate, 1 GPU); shard: "
+                         "propagation microbench (one line per mode and rate; post-bucket shards over the "
+                         "torchrun ranks); shard: "
                          "the 100x network column-sharded over the torchrun ranks; stage0: "
                          "configurations 0 and 1 (one line each, 1 GPU)")
     ap.add_argument("--columns", type=int, default=5000, help="shard workload: columns")

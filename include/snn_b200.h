@@ -141,7 +141,10 @@ typedef struct snn_counters {
     int32_t last_spikes;     /* spikes of the last executed step            */
     int32_t last_byte;       /* byte injected at the last step, -1 = none   */
     double modeled_bytes;    /* algorithmic HBM bytes of the executed steps */
-    int64_t reserved[6];
+    int64_t local_lo;        /* [local_lo, local_hi): the neurons this context
+                                advances (a sharded microbench's post buckets; */
+    int64_t local_hi;        /*  otherwise 0 / n_neurons)                     */
+    int64_t reserved[4];
 } snn_counters;
 
 /* fields for snn_get_state (host_buf gets n elements of the listed type;
@@ -223,6 +226,36 @@ int snn_synchronize(snn_ctx* ctx);
 int snn_get_spikes(snn_ctx* ctx, uint32_t* bitmask, int64_t n_words);
 int snn_get_state(snn_ctx* ctx, int32_t which, void* host_buf, int64_t n_bytes);
 int snn_get_counters(snn_ctx* ctx, snn_counters* out);
+
+/* Semantic evaluation of a Stage 2e network, replacing
+ * BioMechanismScheduler::run_semantic_eval / launch_semantic_eval
+ * (src/stage2e/scheduler.cuh:126, scheduler.cu:785-1036), which the
+ * reference runs every 10,000 steps: the columns' byte responses (the neuron
+ * x byte spike counts summed per column on the device), their pairwise
+ * Jensen-Shannon divergences (natural log; an empty column counts as
+ * uniform), k-means (k 5, JS distance, round-robin start, at most 20
+ * rounds), the silhouette, the column ratio (largest / smallest non-zero
+ * column total), each layer's mean spike delay after the last injection
+ * step before `step`, and each layer's chi-squared byte selectivity (rows
+ * with >= 10 spikes, uniform expectation, df 255, critical 293.2).  Host
+ * arithmetic in double as the reference's; per-neuron chi-squared in float
+ * on the device, each layer's float sum taken in ascending neuron order (the
+ * reference adds them with float atomics, in no fixed order).  Layers are
+ * L4, L2/3, L5, L6, prefrontal.  assign (nullable, n_assign >= columns)
+ * receives each column's cluster.  Not available on sharded contexts. */
+typedef struct snn_semantic {
+    double silhouette, js_mean, js_max, column_ratio, grand_total;
+    int32_t n_columns, nonzero_columns;
+    double layer_delay[5];       /* -1: no neuron of the layer spiked since */
+    int32_t layer_delay_n[5];    /* neurons counted in layer_delay          */
+    int32_t layer_sig[5];        /* rows above the chi-squared critical value */
+    int32_t layer_act[5];        /* rows with >= 10 spikes                  */
+    double layer_chi2_mean[5];   /* float sum / layer_act                   */
+    int32_t reserved[8];
+} snn_semantic;
+int snn_semantic_eval(snn_ctx* ctx, int64_t step, snn_semantic* out, int32_t* assign,
+                      int64_t n_assign);
+
 int snn_set_dopamine(snn_ctx* ctx, float level);
 int snn_set_e0(snn_ctx* ctx, int32_t enable);
 /* Device timing of the engine's kernels: with level 1, CUDA events recorded
@@ -258,7 +291,16 @@ int snn_load(snn_ctx* ctx, const char* path, int32_t fmt);
  * 128-byte ncclUniqueId from snn_nccl_unique_id on one rank, shared with
  * the others by the caller (no counterpart in the reference, which runs on
  * one GPU; replaces its single-device MemoryAllocator,
- * src/stage2e/memory_allocator.cuh:306-339). */
+ * src/stage2e/memory_allocator.cuh:306-339).
+ * The propagation microbench shards by post bucket instead (uid may be
+ * null; nothing is exchanged): rank r advances the neurons
+ * [local_lo, local_hi) of snn_get_counters (the post buckets
+ * [nb r / world, nb (r+1) / world), nb a multiple of world), draws every
+ * forced pre-spike itself and pushes the segments of their rows that land
+ * on its neurons; rasters, neuron state and the weights onto its neurons are
+ * its own (entries of other ranks' neurons stay as built), total_spikes,
+ * arrivals and ltp_visits are local, dispatched is global; sharded
+ * microbench contexts have no checkpoint format. */
 int snn_nccl_unique_id(uint8_t* out, int64_t n);
 int snn_set_shard(snn_ctx* ctx, int32_t rank, int32_t world, const uint8_t* uid, int64_t n);
 /* Host-only partition plan (no GPU): out[0..9] = local neurons, a0, a1, pf0,

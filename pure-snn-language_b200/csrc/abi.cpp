@@ -185,6 +185,14 @@ int snn_get_counters(snn_ctx* ctx, snn_counters* out) {
     return guard(ctx, [&] {
         SNN_REQUIRE(out, SNN_ERR_ARG, "null counters");
         ctx->eng->counters(out);
+        if (out->local_hi == 0) out->local_hi = out->n_neurons;  // unsharded: all neurons
+    });
+}
+
+int snn_semantic_eval(snn_ctx* ctx, int64_t step, snn_semantic* out, int32_t* assign, int64_t n_assign) {
+    return guard(ctx, [&] {
+        SNN_REQUIRE(out, SNN_ERR_ARG, "null result");
+        ctx->eng->semantic_eval(step, out, assign, n_assign);
     });
 }
 
@@ -241,8 +249,10 @@ int snn_nccl_unique_id(uint8_t* out, int64_t n) {
 
 int snn_set_shard(snn_ctx* ctx, int32_t rank, int32_t world, const uint8_t* uid, int64_t n) {
     return guard(ctx, [&] {
-        SNN_REQUIRE(world == 1 || (uid && n >= (int64_t)sizeof(ncclUniqueId)), SNN_ERR_ARG,
-                    "a 128-byte NCCL unique id is needed for world > 1");
+        // Stage 2e needs the id for world > 1 (checked by its engine); the
+        // microbench's post-bucket shards exchange nothing and take none
+        SNN_REQUIRE(!uid || n >= (int64_t)sizeof(ncclUniqueId), SNN_ERR_ARG,
+                    "an NCCL unique id is 128 bytes");
         ctx->eng->set_shard(rank, world, uid);
     });
 }

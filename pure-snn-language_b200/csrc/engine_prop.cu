@@ -69,6 +69,9 @@ struct PDev {
     int nb, bw, parts;        // nb buckets of bw posts; CTAs per bucket in k4_push_b
     int32_t* part;            // [parts][N] sums of the bucketed push, one writer per slot
     int lif_parts;            // > 0: k4_lif sums part[0 .. lif_parts) instead of acc
+    // post range of this rank: buckets [b0, b0 + nb_loc), neurons [lo, hi)
+    // (one GPU: the whole network); `sharded` counts events per local segment
+    int b0, nb_loc, lo, hi, sharded;
 };
 
 __device__ __forceinline__ float e20(const PDev& D, int dt) {
@@ -309,10 +312,10 @@ __global__ void __launch_bounds__(B_THREADS) k4_push_b(PDev D, int k) {
     if (blockIdx.x == 0 && threadIdx.x == 0) {
         C->n_pre[par ^ 1] = 0;
         C->n_post = 0;
-        C->events += (unsigned long long)n * (unsigned)D.F;
+        if (!D.sharded) C->events += (unsigned long long)n * (unsigned)D.F;
         C->pre_spikes += n;
     }
-    const int b = blockIdx.x % D.nb, p = blockIdx.x / D.nb;
+    const int b = D.b0 + blockIdx.x % D.nb_loc, p = blockIdx.x / D.nb_loc;
     const int lo_post = b * D.bw;
     const int width = min(D.bw, D.N - lo_post);
     // with STDP the bucket's last post spikes follow the slots in shared
@@ -334,6 +337,7 @@ __global__ void __launch_bounds__(B_THREADS) k4_push_b(PDev D, int k) {
     const float* rl = D.rel_list + (size_t)par * D.N;
     const int nb1 = D.nb + 1;
     int i_n[B_SP], o0_n[B_SP], o1_n[B_SP];
+    unsigned n_ev = 0;  // events of this group's segments (sharded runs count them)
     long long e = e_lo + slot;
 #pragma unroll
     for (int sp = 0; sp < B_SP; ++sp) {
@@ -368,11 +372,12 @@ __global__ void __launch_bounds__(B_THREADS) k4_push_b(PDev D, int k) {
             const long long es = e + (long long)sp * nslots;
             const bool valid = es < e_hi;
             rel[sp] = STP && valid ? rl[es] : 1.0f;
-            if ((STDP || STP) && valid && b == 0 && gl == 0)
+            if ((STDP || STP) && valid && b == D.b0 && gl == 0)
                 commit_spike<STDP, STP>(D, i[sp], (size_t)par * D.N + es, t);
             base[sp] = (long long)i[sp] * D.F;
             plastic[sp] = learn && i[sp] < D.n_exc;
             if (!valid) o1[sp] = o0[sp];  // empty segment
+            if (gl == 0) n_ev += (unsigned)(o1[sp] - o0[sp]);
         }
         // first B_G * B_U synapses of every segment, all loads in flight together
         int q[B_SP][B_U];
@@ -404,6 +409,11 @@ __global__ void __launch_bounds__(B_THREADS) k4_push_b(PDev D, int k) {
                 push_b_chunk<STDP, STP>(D, j0, o1[sp], base[sp], lo_post, acc_s, lp_s, rel[sp], plastic[sp], t,
                                         lr);
     }
+    if (D.sharded) {  // events = the rank's segments of the spikers' rows
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) n_ev += __shfl_xor_sync(0xffffffffu, n_ev, o);
+        if ((threadIdx.x & 31) == 0 && n_ev) atomicAdd(&C->events, (unsigned long long)n_ev);
+    }
     __syncthreads();
     int32_t* out = D.part + (size_t)p * D.N + lo_post;
     for (int x = threadIdx.x; x < width; x += B_THREADS) out[x] = acc_s[x];
@@ -416,7 +426,7 @@ __global__ void __launch_bounds__(P_THREADS) k4_lif(PDev D, int k) {
     const int j = blockIdx.x * P_THREADS + threadIdx.x;
     const int lane = threadIdx.x & 31;
     bool sp = false;
-    if (j < D.N) {
+    if (j >= D.lo && j < D.hi) {  // this rank's posts (one GPU: all)
         // this step's input: the accumulator of the direct push (consumed
         // and cleared), or the per-part sums of the bucketed push (int32
         // addition: the same value in any order)
@@ -645,6 +655,7 @@ struct EngineProp : snnb::Engine {
     int push_grid = 1, lif_grid = 1, ltp_grid = 1;
     uint32_t max_in = 0, spec_seed = 0;
     float dopamine = 1.0f;
+    int rank = 0, world = 1;  // post-bucket shards (snn_set_shard)
     snnb::DevBuf<int32_t> post, acc, last_post, tA, tB, pre_list, post_list, part;
     snnb::DevBuf<float> w, V, I, u, R, rel_list, un_list, rn_list, exp_tab;
     snnb::DevBuf<int8_t> ref;
@@ -687,6 +698,20 @@ struct EngineProp : snnb::Engine {
 
     int nkern() const { return stdp ? 3 : 2; }
 
+    // Sharding over `w` GPUs by post bucket: rank r owns the buckets
+    // [nb r / w, nb (r + 1) / w) (nb a multiple of w) and their neurons.  The
+    // forced pre-spikes are a seeded hash of (step, neuron), so every rank
+    // draws all of them and pushes the segments of their rows that fall in
+    // its buckets; LIF, LTD (the post's last spike) and LTP (the incoming
+    // synapses of a local post spike) only touch local posts, so no data
+    // crosses GPUs during the run.  No NCCL communicator is needed.
+    void set_shard(int32_t r, int32_t w, const void*) override {
+        SNN_REQUIRE(!built, SNN_ERR_STATE, "shard before building the network");
+        SNN_REQUIRE(w >= 1 && r >= 0 && r < w, SNN_ERR_ARG, "bad rank / world size");
+        rank = r;
+        world = w;
+    }
+
     void build(const snn_topology_spec& spec) override {
         SNN_REQUIRE(!built, SNN_ERR_STATE, "network already built");
         SNN_CUDA(cudaSetDevice(cfg.device));
@@ -722,6 +747,11 @@ struct EngineProp : snnb::Engine {
         SNN_REQUIRE(cfg.prop_push >= 0 && cfg.prop_push <= 2, SNN_ERR_ARG, "prop_push must be 0, 1 or 2");
         SNN_REQUIRE(cfg.prop_push != 2 || sorted, SNN_ERR_ARG,
                     "bucketed push needs at most 256 post buckets and fan-out <= 65535");
+        SNN_REQUIRE(world == 1 || (sorted && cfg.prop_push != 1), SNN_ERR_ARG,
+                    "a sharded microbench needs the bucketed push (at most 256 post buckets, "
+                    "fan-out <= 65535, prop_push 0 or 2)");
+        SNN_REQUIRE(world == 1 || (long long)N >= 2ll * world, SNN_ERR_ARG,
+                    "a sharded microbench needs at least two neurons per rank");
         D.nb = nb_min;
         D.bw = (int)(((long long)N + nb_min - 1) / nb_min);
         D.parts = 1;
@@ -732,7 +762,11 @@ struct EngineProp : snnb::Engine {
             struct Cand { int nb, bw, parts; double util; };
             std::vector<Cand> cands;
             double best = 0.0;
-            for (int nb = nb_min; nb <= std::min(256, std::max(2 * nb_min, nb_min + 8)); ++nb) {
+            // sharded: nb a multiple of the world size, each rank's nb / world
+            // buckets x parts CTAs filling its SMs
+            const int nb_hi = std::min(256, std::max(2 * nb_min, nb_min + 8) + (world > 1 ? 2 * world : 0));
+            for (int nb = nb_min; nb <= nb_hi; ++nb) {
+                if (nb % world != 0) continue;
                 const int bw = (int)(((long long)N + nb - 1) / nb);
                 if ((int)(((long long)N + bw - 1) / bw) != nb) continue;  // nb buckets of bw cover N
                 int occ = 0;
@@ -740,8 +774,9 @@ struct EngineProp : snnb::Engine {
                                                                        (size_t)slot_bytes * bw));
                 if (occ < 1) continue;
                 const int slots = occ * dev_sms;
-                const int parts = std::max(1, slots / nb);
-                const long long ctas = (long long)nb * parts;
+                const int nb_loc = nb / world;
+                const int parts = std::max(1, slots / nb_loc);
+                const long long ctas = (long long)nb_loc * parts;
                 const double util = (double)ctas / (double)(((ctas + slots - 1) / slots) * slots);
                 cands.push_back({nb, bw, parts, util});
                 best = std::max(best, util);
@@ -760,8 +795,15 @@ struct EngineProp : snnb::Engine {
         // at 1M x 1,000: the bucketed step is faster from 0.1 % forced rate
         // up, 1.4x at 1 %, 2.7x at 10 %; the direct push only wins, by ~1 %,
         // at 0.1 % with STDP)
-        bucketed = cfg.prop_push == 2 ||
+        bucketed = cfg.prop_push == 2 || world > 1 ||
                    (cfg.prop_push == 0 && sorted && (double)cfg.prop_rate * F >= 1.0);
+        D.sharded = world > 1;
+        D.nb_loc = D.nb / world;
+        D.b0 = rank * D.nb_loc;
+        D.lo = D.b0 * D.bw;
+        D.hi = (int)std::min<long long>(N, (long long)(D.b0 + D.nb_loc) * D.bw);
+        SNN_REQUIRE(D.nb % world == 0 && D.lo < D.hi, SNN_ERR_ARG,
+                    "no post-bucket layout gives every rank a share of the neurons");
 
         post.alloc(S);
         w.alloc(S);
@@ -890,7 +932,7 @@ struct EngineProp : snnb::Engine {
     void launch_step(int k, cudaEvent_t* ev, bool capturing) {
         const unsigned fl = capturing ? cudaEventRecordExternal : cudaEventRecordDefault;
         if (ev) SNN_CUDA(cudaEventRecordWithFlags(ev[0], stream, fl));
-        if (bucketed) push_kernel_b()<<<D.nb * D.parts, B_THREADS, push_smem, stream>>>(D, k);
+        if (bucketed) push_kernel_b()<<<D.nb_loc * D.parts, B_THREADS, push_smem, stream>>>(D, k);
         else if (vec) push_kernel()<<<push_grid, P_THREADS, 0, stream>>>(D, k);
         else push_kernel_scalar()<<<push_grid, P_THREADS, 0, stream>>>(D, k);
         if (ev) SNN_CUDA(cudaEventRecordWithFlags(ev[1], stream, fl));
@@ -1024,6 +1066,8 @@ struct EngineProp : snnb::Engine {
         o->ltp_visits = (int64_t)h.ltp_visits;
         o->n_neurons = D.N;
         o->n_synapses = S;
+        o->local_lo = D.lo;
+        o->local_hi = D.hi;
         o->last_byte = -1;
         if (steps > 0) {
             std::vector<uint32_t> row(D.words);
@@ -1137,12 +1181,14 @@ struct EngineProp : snnb::Engine {
     void save(const char* path, int32_t fmt) override {
         SNN_REQUIRE(built, SNN_ERR_STATE, "build the network first");
         SNN_REQUIRE(fmt == SNN_FMT_NATIVE, SNN_ERR_UNSUPPORTED, "the microbench writes the native format only");
+        SNN_REQUIRE(world == 1, SNN_ERR_UNSUPPORTED, "a sharded microbench has no checkpoint format");
         const NativeBlob b = blob();
         snnb::save_native(path, SNN_MODEL_PROP, &b, sizeof(b), native_sections(), stream);
     }
     void load(const char* path, int32_t fmt) override {
         SNN_REQUIRE(built, SNN_ERR_STATE, "build the network first");
         SNN_REQUIRE(fmt == SNN_FMT_NATIVE, SNN_ERR_UNSUPPORTED, "the microbench reads the native format only");
+        SNN_REQUIRE(world == 1, SNN_ERR_UNSUPPORTED, "a sharded microbench has no checkpoint format");
         const NativeBlob want = blob();
         NativeBlob got{};
         snnb::load_native(path, SNN_MODEL_PROP, &got, sizeof(got), native_sections(), stream,

@@ -75,10 +75,29 @@ class Counters(C.Structure):
                 ("ltp_visits", C.c_int64), ("burst_spikes", C.c_int64),
                 ("n_neurons", C.c_int64), ("n_synapses", C.c_int64), ("n_groups", C.c_int64),
                 ("last_spikes", C.c_int32), ("last_byte", C.c_int32),
-                ("modeled_bytes", C.c_double), ("reserved", C.c_int64 * 6)]
+                ("modeled_bytes", C.c_double), ("local_lo", C.c_int64), ("local_hi", C.c_int64),
+                ("reserved", C.c_int64 * 4)]
 
     def as_dict(self):
         return {k: getattr(self, k) for k, _ in self._fields_ if k != "reserved"}
+
+
+class Semantic(C.Structure):
+    _fields_ = [("silhouette", C.c_double), ("js_mean", C.c_double), ("js_max", C.c_double),
+                ("column_ratio", C.c_double), ("grand_total", C.c_double),
+                ("n_columns", C.c_int32), ("nonzero_columns", C.c_int32),
+                ("layer_delay", C.c_double * 5), ("layer_delay_n", C.c_int32 * 5),
+                ("layer_sig", C.c_int32 * 5), ("layer_act", C.c_int32 * 5),
+                ("layer_chi2_mean", C.c_double * 5), ("reserved", C.c_int32 * 8)]
+
+    def as_dict(self):
+        out = {}
+        for k, _ in self._fields_:
+            if k == "reserved":
+                continue
+            v = getattr(self, k)
+            out[k] = list(v) if hasattr(v, "__len__") else v
+        return out
 
 
 class Profile(C.Structure):
@@ -99,7 +118,7 @@ EXPORTS = ["snn_config_init", "snn_topology_init", "snn_create", "snn_destroy",
            "snn_run", "snn_synchronize", "snn_get_spikes", "snn_get_state", "snn_get_counters",
            "snn_set_dopamine", "snn_set_e0", "snn_save", "snn_load", "snn_stream_generate",
            "snn_set_profiling", "snn_get_profile", "snn_propagate", "snn_propagate_static",
-           "snn_nccl_unique_id", "snn_set_shard", "snn_shard_plan"]
+           "snn_nccl_unique_id", "snn_set_shard", "snn_shard_plan", "snn_semantic_eval"]
 
 _lib = None
 
@@ -128,6 +147,7 @@ def lib():
         L.snn_get_spikes.argtypes = [vp, vp, C.c_int64]
         L.snn_get_state.argtypes = [vp, C.c_int32, vp, C.c_int64]
         L.snn_get_counters.argtypes = [vp, C.POINTER(Counters)]
+        L.snn_semantic_eval.argtypes = [vp, C.c_int64, C.POINTER(Semantic), vp, C.c_int64]
         L.snn_set_dopamine.argtypes = [vp, C.c_float]
         L.snn_set_e0.argtypes = [vp, C.c_int32]
         L.snn_save.argtypes = [vp, C.c_char_p, C.c_int32]
@@ -306,6 +326,19 @@ class Network:
         c = Counters()
         self._check(self.L.snn_get_counters(self.h, C.byref(c)))
         return c.as_dict()
+
+    def semantic_eval(self, step=None):
+        """Semantic evaluation of a Stage 2e network (snn_semantic_eval):
+        dict of the scalars and per-layer lists, plus each column's cluster
+        under "assign".  step defaults to the number of executed steps."""
+        out = Semantic()
+        n_col = max(int(getattr(self, "n_columns", 0) or 0), 1)
+        asg = np.zeros(n_col, np.int32)
+        st = self.counters()["step"] if step is None else int(step)
+        self._check(self.L.snn_semantic_eval(self.h, st, C.byref(out), asg.ctypes.data, asg.size))
+        d = out.as_dict()
+        d["assign"] = asg[: d["n_columns"]]
+        return d
 
     def set_profiling(self, enable=True):
         """True / 1: per-kernel device times; 2: whole-run device time only
