@@ -96,6 +96,13 @@ public:
     long long dispatched_events_accum() const { return counters().dispatched; }
     long long dropped_events_accum() const { return counters().dropped_ref; }
     int total_single_neuron_burst_spikes() const { return (int)counters().burst_spikes; }
+    // run_semantic_eval (src/stage2e/scheduler.cuh:126): the result instead
+    // of the reference's cached members (p3_silhouette_score_, ...)
+    snn_semantic run_semantic_eval(int step) const {
+        snn_semantic r;
+        detail::check(snn_semantic_eval(h_.ctx, step, &r, nullptr, 0), h_.ctx, "snn_semantic_eval");
+        return r;
+    }
 
     template <typename T>
     std::vector<T> state(int32_t which, size_t n) const {

@@ -409,3 +409,131 @@ def propagate(post, w, fanout, spikes, n_post, frac_bits=24):
     L.o4_propagate(post.ctypes.data, w.ctypes.data, len(spikes), fanout, spikes.ctypes.data,
                    acc.ctypes.data, frac_bits)
     return acc
+
+
+def semantic_eval(nbc, last, region, n_columns, npc, step):
+    """Semantic evaluation of a Stage 2e network, restated from
+    BioMechanismScheduler::launch_semantic_eval (src/stage2e/scheduler.cu:
+    785-1036) with the js_divergence helper (:31-40), the column response
+    kernel (:294-310) and the per-neuron chi-squared kernel (:195-231).
+    Plain Python loops in the reference's order of operations (math.log is
+    the C library's log), the per-neuron chi-squared in float32 and each
+    layer's float sum in ascending neuron order.  nbc: int32[N, 256] neuron x
+    byte spike counts; last: int32[N] last spike step; region: uint8[N]
+    (0 L4, 1 L2/3, 2 L5, 3 L6, 4 prefrontal)."""
+    import math
+    NB, K = 256, 5
+    nbc = np.asarray(nbc, np.int64).reshape(-1, NB)
+    resp = nbc[: n_columns * npc].reshape(n_columns, npc, NB).sum(axis=1)
+    P, col_total, grand = [], [], 0.0
+    for c in range(n_columns):
+        s = 0.0
+        for b in range(NB):
+            s += float(resp[c, b])
+        col_total.append(s)
+        grand += s
+        P.append([1.0 / NB] * NB if s < 1e-10 else [float(resp[c, b]) / s for b in range(NB)])
+
+    def js(p, q):
+        v = 0.0
+        for b in range(NB):
+            m = 0.5 * (p[b] + q[b])
+            if p[b] > 1e-12 and m > 1e-12:
+                v += 0.5 * p[b] * math.log(p[b] / m)
+            if q[b] > 1e-12 and m > 1e-12:
+                v += 0.5 * q[b] * math.log(q[b] / m)
+        return 0.0 if v < 0.0 else v
+
+    jm = [[0.0] * n_columns for _ in range(n_columns)]
+    js_sum, js_max, js_n = 0.0, 0.0, 0
+    for i in range(n_columns):
+        for j in range(i + 1, n_columns):
+            v = js(P[i], P[j])
+            jm[i][j] = jm[j][i] = v
+            js_sum += v
+            js_max = max(js_max, v)
+            js_n += 1
+    asg = [i % K for i in range(n_columns)]
+    for _ in range(20):
+        cnt, sp = [0] * K, [[0.0] * NB for _ in range(K)]
+        for i in range(n_columns):
+            cnt[asg[i]] += 1
+            for b in range(NB):
+                sp[asg[i]][b] += P[i][b]
+        cen = []
+        for k in range(K):
+            if cnt[k] > 0:
+                ck, s = [], 0.0
+                for b in range(NB):
+                    ck.append(sp[k][b] / cnt[k])
+                    s += ck[b]
+                cen.append([1.0 / NB] * NB if s < 1e-12 else [x / s for x in ck])
+            else:
+                cen.append([1.0 / NB] * NB)
+        changed = False
+        for i in range(n_columns):
+            best, bk = float("inf"), 0
+            for k in range(K):
+                d = js(P[i], cen[k])
+                if d < best:
+                    best, bk = d, k
+            if bk != asg[i]:
+                asg[i], changed = bk, True
+        if not changed:
+            break
+    sil, sil_n = 0.0, 0
+    for i in range(n_columns):
+        a, an, bmin = 0.0, 0, float("inf")
+        for k in range(K):
+            if k == asg[i]:
+                for j in range(n_columns):
+                    if j != i and asg[j] == k:
+                        a += jm[i][j]
+                        an += 1
+                if an > 0:
+                    a /= an
+            else:
+                ds, dn = 0.0, 0
+                for j in range(n_columns):
+                    if asg[j] == k:
+                        ds += jm[i][j]
+                        dn += 1
+                if dn > 0 and ds / dn < bmin:
+                    bmin = ds / dn
+        if an > 0 and bmin < float("inf"):
+            den = max(a, bmin)
+            sil += (bmin - a) / den if den > 1e-12 else 0.0
+            sil_n += 1
+    nzt = [t for t in col_total if t > 0.0]
+    li = max(((step - 1) // 3) * 3, 0) if step >= 1 else 0
+    tot = nbc.sum(axis=1)
+    expected = tot.astype(np.float32) * np.float32(1.0 / 256.0)
+    chi = np.zeros(nbc.shape[0], np.float32)
+    for b in range(NB):
+        diff = nbc[:, b].astype(np.float32) - expected
+        chi = chi + (diff * diff) / np.where(expected < 1e-10, np.float32(1), expected)
+    chi = np.where(expected < 1e-10, np.float32(0), chi).astype(np.float32)
+    out = {"js_mean": js_sum / js_n if js_n else 0.0, "js_max": js_max,
+           "silhouette": sil / sil_n if sil_n else 0.0, "grand_total": grand,
+           "nonzero_columns": len(nzt), "n_columns": n_columns,
+           "column_ratio": max(nzt) / min(nzt) if len(nzt) >= 2 else 0.0, "assign": asg,
+           "layer_delay": [], "layer_delay_n": [], "layer_sig": [], "layer_act": [],
+           "layer_chi2_mean": []}
+    region = np.asarray(region)
+    last = np.asarray(last, np.int64)
+    for r in range(5):
+        sel = np.nonzero(region == r)[0]
+        hit = sel[last[sel] >= li]
+        out["layer_delay_n"].append(int(hit.size))
+        d = 0.0
+        for i in hit:
+            d += float(last[i] - li)
+        out["layer_delay"].append(d / hit.size if hit.size else -1.0)
+        act = sel[tot[sel] >= 10]
+        cs = np.float32(0)
+        for i in act:
+            cs = np.float32(cs + chi[i])
+        out["layer_act"].append(int(act.size))
+        out["layer_sig"].append(int((chi[act] > np.float32(293.2)).sum()))
+        out["layer_chi2_mean"].append(float(cs) / act.size if act.size else 0.0)
+    return out

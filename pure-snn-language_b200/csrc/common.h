@@ -86,6 +86,9 @@ struct Engine {
     virtual void set_profiling(int32_t) { throw Error(SNN_ERR_UNSUPPORTED, "profiling not available"); }
     virtual void get_profile(snn_profile*) { throw Error(SNN_ERR_UNSUPPORTED, "profiling not available"); }
     virtual void sync() = 0;
+    virtual void semantic_eval(int64_t, snn_semantic*, int32_t*, int64_t) {
+        throw Error(SNN_ERR_UNSUPPORTED, "semantic evaluation exists for the Stage 2e network only");
+    }
 };
 
 Engine* make_engine_stage2e(const snn_config& cfg);

@@ -38,6 +38,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <limits>
 #include <memory>
 #include <nccl.h>
 #include "nccl_dl.h"
@@ -1043,6 +1044,60 @@ __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d,
 }
 
 // ---------------------------------------------------------------------------
+// semantic evaluation (src/stage2e/scheduler.cu:294-310 and :195-231): the
+// columns' byte responses, one CTA per column, thread b adding byte b over
+// the column's contiguous neurons (exact int sums); each neuron's spike total
+// and chi-squared against the uniform expectation, in float, in the
+// reference's order of operations
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) k_column_bytes(const int* __restrict__ nbc, int npc, int* __restrict__ out) {
+    const int c = blockIdx.x, b = threadIdx.x;
+    const int* src = nbc + (size_t)c * npc * 256 + b;
+    int sum = 0;
+    for (int i = 0; i < npc; ++i) sum += src[(size_t)i * 256];
+    out[(size_t)c * 256 + b] = sum;
+}
+
+__global__ void __launch_bounds__(256) k_neuron_chi2(const int* __restrict__ nbc, int N, float* __restrict__ chi2,
+                                                     int* __restrict__ total) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= N) return;
+    const int4* row = reinterpret_cast<const int4*>(nbc + (size_t)i * 256);
+    int rt = 0;
+    for (int q = 0; q < 64; ++q) {
+        const int4 v = row[q];
+        rt += v.x + v.y + v.z + v.w;
+    }
+    const float expected = pm_mul(pm_i2f(rt), 1.0f / 256.0f);
+    float x = 0.0f;
+    if (!(expected < 1e-10f))
+        for (int q = 0; q < 64; ++q) {
+            const int4 v = row[q];
+            const int c4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const float diff = pm_sub(pm_i2f(c4[u]), expected);
+                x = pm_add(x, pm_div(pm_mul(diff, diff), expected));
+            }
+        }
+    chi2[i] = x;
+    total[i] = rt;
+}
+
+// Jensen-Shannon divergence of two distributions over `dim` bins, natural log
+// (src/stage2e/scheduler.cu:31-40)
+static double js_div(const double* P, const double* Q, int dim) {
+    double js = 0.0;
+    for (int b = 0; b < dim; ++b) {
+        const double pi = P[b], pj = Q[b];
+        const double m = 0.5 * (pi + pj);
+        if (pi > 1e-12 && m > 1e-12) js += 0.5 * pi * std::log(pi / m);
+        if (pj > 1e-12 && m > 1e-12) js += 0.5 * pj * std::log(pj / m);
+    }
+    return js < 0.0 ? 0.0 : js;
+}
+
+// ---------------------------------------------------------------------------
 // host engine
 // ---------------------------------------------------------------------------
 struct Engine2e : snnb::Engine {
@@ -1694,6 +1749,154 @@ struct Engine2e : snnb::Engine {
         b.download(h.data(), n, stream);
         SNN_CUDA(cudaStreamSynchronize(stream));
         return h;
+    }
+
+    // BioMechanismScheduler::launch_semantic_eval (src/stage2e/scheduler.cu:785-1036)
+    void semantic_eval(int64_t step, snn_semantic* o, int32_t* assign_out, int64_t n_assign) override {
+        SNN_REQUIRE(built, SNN_ERR_STATE, "build the network first");
+        SNN_REQUIRE(world == 1, SNN_ERR_UNSUPPORTED, "semantic evaluation of a sharded network is not available");
+        const int NC = net.ncol, NB = 256, N = D.N;
+        SNN_REQUIRE(NC >= 1, SNN_ERR_STATE, "the network has no columns");
+        SNN_REQUIRE(!assign_out || n_assign >= NC, SNN_ERR_ARG, "cluster buffer smaller than the column count");
+        snnb::DevBuf<int> d_col, d_tot;
+        snnb::DevBuf<float> d_chi;
+        d_col.alloc((size_t)NC * NB);
+        d_tot.alloc(N);
+        d_chi.alloc(N);
+        k_column_bytes<<<NC, NB, 0, stream>>>(neuron_byte_counts.p, D.NPC, d_col.p);
+        k_neuron_chi2<<<(N + 255) / 256, 256, 0, stream>>>(neuron_byte_counts.p, N, d_chi.p, d_tot.p);
+        SNN_CUDA(cudaGetLastError());
+        const std::vector<int> resp = fetch(d_col, (size_t)NC * NB);
+        const std::vector<int> tot = fetch(d_tot, N);
+        const std::vector<float> chi = fetch(d_chi, N);
+        const std::vector<int> lst = fetch(last, N);
+        memset(o, 0, sizeof(*o));
+        o->n_columns = NC;
+        // column distributions (an empty column counts as uniform)
+        std::vector<double> P((size_t)NC * NB), col_total(NC, 0.0);
+        double grand = 0.0;
+        for (int c = 0; c < NC; ++c) {
+            double sum = 0.0;
+            for (int b = 0; b < NB; ++b) sum += resp[(size_t)c * NB + b];
+            col_total[c] = sum;
+            grand += sum;
+            for (int b = 0; b < NB; ++b)
+                P[(size_t)c * NB + b] = sum < 1e-10 ? 1.0 / NB : resp[(size_t)c * NB + b] / sum;
+        }
+        o->grand_total = grand;
+        // pairwise JS
+        std::vector<double> js((size_t)NC * NC, 0.0);
+        double js_sum = 0.0, js_max = 0.0;
+        long long js_n = 0;
+        for (int i = 0; i < NC; ++i)
+            for (int j = i + 1; j < NC; ++j) {
+                const double v = js_div(&P[(size_t)i * NB], &P[(size_t)j * NB], NB);
+                js[(size_t)i * NC + j] = js[(size_t)j * NC + i] = v;
+                js_sum += v;
+                if (v > js_max) js_max = v;
+                ++js_n;
+            }
+        o->js_mean = js_n > 0 ? js_sum / js_n : 0.0;
+        o->js_max = js_max;
+        // k-means, k 5, JS distance, round-robin start
+        const int K = 5;
+        std::vector<int> asg(NC);
+        for (int i = 0; i < NC; ++i) asg[i] = i % K;
+        std::vector<double> cen((size_t)K * NB);
+        for (int iter = 0; iter < 20; ++iter) {
+            std::vector<int> cnt(K, 0);
+            std::vector<double> sp((size_t)K * NB, 0.0);
+            for (int i = 0; i < NC; ++i) {
+                cnt[asg[i]]++;
+                for (int b = 0; b < NB; ++b) sp[(size_t)asg[i] * NB + b] += P[(size_t)i * NB + b];
+            }
+            for (int k = 0; k < K; ++k) {
+                double* ck = &cen[(size_t)k * NB];
+                if (cnt[k] > 0) {
+                    double sum = 0.0;
+                    for (int b = 0; b < NB; ++b) {
+                        ck[b] = sp[(size_t)k * NB + b] / cnt[k];
+                        sum += ck[b];
+                    }
+                    for (int b = 0; b < NB; ++b) ck[b] = sum < 1e-12 ? 1.0 / NB : ck[b] / sum;
+                } else {
+                    for (int b = 0; b < NB; ++b) ck[b] = 1.0 / NB;
+                }
+            }
+            bool changed = false;
+            for (int i = 0; i < NC; ++i) {
+                double best = std::numeric_limits<double>::max();
+                int bk = 0;
+                for (int k = 0; k < K; ++k) {
+                    const double dd = js_div(&P[(size_t)i * NB], &cen[(size_t)k * NB], NB);
+                    if (dd < best) { best = dd; bk = k; }
+                }
+                if (bk != asg[i]) { asg[i] = bk; changed = true; }
+            }
+            if (!changed) break;
+        }
+        // silhouette on the JS matrix
+        double sil = 0.0;
+        int sil_n = 0;
+        for (int i = 0; i < NC; ++i) {
+            double a = 0.0, bmin = std::numeric_limits<double>::max();
+            int an = 0;
+            for (int k = 0; k < K; ++k) {
+                if (k == asg[i]) {
+                    for (int j = 0; j < NC; ++j)
+                        if (j != i && asg[j] == k) { a += js[(size_t)i * NC + j]; ++an; }
+                    if (an > 0) a /= an;
+                } else {
+                    double ds = 0.0;
+                    int dn = 0;
+                    for (int j = 0; j < NC; ++j)
+                        if (asg[j] == k) { ds += js[(size_t)i * NC + j]; ++dn; }
+                    if (dn > 0 && ds / dn < bmin) bmin = ds / dn;
+                }
+            }
+            if (an > 0 && bmin < std::numeric_limits<double>::max()) {
+                const double den = a > bmin ? a : bmin;
+                sil += den > 1e-12 ? (bmin - a) / den : 0.0;
+                ++sil_n;
+            }
+        }
+        o->silhouette = sil_n > 0 ? sil / sil_n : 0.0;
+        // column ratio over the non-zero columns
+        double cmin = std::numeric_limits<double>::max(), cmax = 0.0;
+        int nz = 0;
+        for (int c = 0; c < NC; ++c)
+            if (col_total[c] > 0.0) {
+                cmin = std::min(cmin, col_total[c]);
+                cmax = std::max(cmax, col_total[c]);
+                ++nz;
+            }
+        o->nonzero_columns = nz;
+        o->column_ratio = (nz >= 2 && cmin > 0.0) ? cmax / cmin : 0.0;
+        // per layer: mean spike delay after the last injection step before
+        // `step`, and chi-squared selectivity (float sums in neuron order)
+        long long li = ((step - 1) / 3) * 3;
+        if (li < 0) li = 0;
+        double dsum[5] = {0, 0, 0, 0, 0};
+        float csum[5] = {0, 0, 0, 0, 0};
+        for (int i = 0; i < N; ++i) {
+            const int r = net.region[i];
+            if (r > 4) continue;
+            if (lst[i] >= li) {
+                dsum[r] += (double)(lst[i] - li);
+                o->layer_delay_n[r]++;
+            }
+            if (tot[i] >= 10) {
+                o->layer_act[r]++;
+                csum[r] = pm_add(csum[r], chi[i]);
+                if (chi[i] > 293.2f) o->layer_sig[r]++;
+            }
+        }
+        for (int r = 0; r < 5; ++r) {
+            o->layer_delay[r] = o->layer_delay_n[r] > 0 ? dsum[r] / o->layer_delay_n[r] : -1.0;
+            o->layer_chi2_mean[r] = o->layer_act[r] > 0 ? (double)csum[r] / (double)o->layer_act[r] : 0.0;
+        }
+        if (assign_out)
+            for (int i = 0; i < NC; ++i) assign_out[i] = asg[i];
     }
 
     void get_state(int32_t which, void* buf, int64_t nbytes) override {
