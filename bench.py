@@ -292,7 +292,7 @@ def prop_main(args):
                            "ltp_visits_per_step": ltp_v / args.steps,
                            "parallelism": f"post-bucket shards x{world}" if world > 1 else "1 GPU",
                            "exchange": "none during the run (forced pre-spikes drawn on every rank)",
-                           "l2": "inputs larger than L2 (8 GB of synapse streams)"},
+                           "l2": f"inputs larger than L2 ({n_neu * 8e-6:.1f} GB of synapse streams)"},
                 "e2e": {"value": e2e_ev / wall, "unit": UNIT, "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": net.words * 4},
                 "gpu_launches": int(sum(v["launches"] for v in prof["kernels"].values())),

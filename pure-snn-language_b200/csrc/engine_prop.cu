@@ -90,6 +90,16 @@ __device__ __forceinline__ float ltd(const PDev& D, float w, int q, int t, float
     return ltd_lp(D, w, __ldcg(D.last_post + q), t, lr);
 }
 
+// the same, from the post's age t - lp kept in 16 bits by the bucketed push
+// (SNN_PROP_AGE_NONE: never spiked, or older than the table, where
+// exp(-dt/20) is 0 and the weight, which lies in [0, w_max], stays as it is)
+constexpr unsigned SNN_PROP_AGE_NONE = 0xFFFFu;
+__device__ __forceinline__ float ltd_age(const PDev& D, float w, unsigned age, float lr) {
+    if (age > SNN_PROP_EXP_STEPS) return w;
+    const float dw = pm_mul(-0.05f, __ldg(D.exp_tab + age));
+    return pm_min(pm_max(pm_fma(lr, dw, w), 0.0f), D.w_max);
+}
+
 // warp-aggregated append of flagged lanes to list[] (count at *cnt)
 __device__ __forceinline__ unsigned warp_append(bool flag, unsigned* cnt, int lane) {
     const unsigned m = __ballot_sync(0xffffffffu, flag);
@@ -280,7 +290,7 @@ constexpr int B_SP = SNN_B_SP;
 
 template <bool STDP, bool STP>
 __device__ __forceinline__ void push_b_chunk(const PDev& D, int j0, int o1, long long base, int lo_post,
-                                             int* acc_s, const int* lp_s, float rel, bool plastic, int t,
+                                             int* acc_s, const uint16_t* age_s, float rel, bool plastic, int t,
                                              float lr) {
     int q[B_U];
     float wv[B_U];
@@ -297,7 +307,7 @@ __device__ __forceinline__ void push_b_chunk(const PDev& D, int j0, int o1, long
         const int j = j0 + u * B_G;
         if (j < o1) {
             atomicAdd(acc_s + (q[u] - lo_post), snn_prop_quant(wv[u], rel, STP));
-            if (plastic) D.w[base + j] = ltd_lp(D, wv[u], lp_s[q[u] - lo_post], t, lr);
+            if (plastic) D.w[base + j] = ltd_age(D, wv[u], age_s[q[u] - lo_post], lr);
         }
     }
 }
@@ -318,13 +328,17 @@ __global__ void __launch_bounds__(B_THREADS) k4_push_b(PDev D, int k) {
     const int b = D.b0 + blockIdx.x % D.nb_loc, p = blockIdx.x / D.nb_loc;
     const int lo_post = b * D.bw;
     const int width = min(D.bw, D.N - lo_post);
-    // with STDP the bucket's last post spikes follow the slots in shared
-    // memory, so that the fused LTD reads them there
-    int* const lp_s = acc_s + D.bw;
+    // with STDP the age of each post's last spike (16 bits) follows the
+    // slots in shared memory, so that the fused LTD reads it there and a slot
+    // costs 6 bytes (wider buckets, longer row segments)
+    uint16_t* const age_s = reinterpret_cast<uint16_t*>(acc_s + D.bw);
     const bool learn_s = STDP && C->learn;
     for (int x = threadIdx.x; x < width; x += B_THREADS) {
         acc_s[x] = 0;
-        if (learn_s) lp_s[x] = __ldcg(D.last_post + lo_post + x);
+        if (learn_s) {
+            const int lp = __ldcg(D.last_post + lo_post + x);
+            age_s[x] = (lp < 0 || t - lp > SNN_PROP_EXP_STEPS) ? (uint16_t)SNN_PROP_AGE_NONE : (uint16_t)(t - lp);
+        }
     }
     __syncthreads();
     const long long e_lo = (long long)n * p / D.parts, e_hi = (long long)n * (p + 1) / D.parts;
@@ -399,14 +413,14 @@ __global__ void __launch_bounds__(B_THREADS) k4_push_b(PDev D, int k) {
                 const int j = o0[sp] + gl + u * B_G;
                 if (j < o1[sp]) {
                     atomicAdd(acc_s + (q[sp][u] - lo_post), snn_prop_quant(wv[sp][u], rel[sp], STP));
-                    if (plastic[sp]) D.w[base[sp] + j] = ltd_lp(D, wv[sp][u], lp_s[q[sp][u] - lo_post], t, lr);
+                    if (plastic[sp]) D.w[base[sp] + j] = ltd_age(D, wv[sp][u], age_s[q[sp][u] - lo_post], lr);
                 }
             }
         // rare long segments
 #pragma unroll
         for (int sp = 0; sp < B_SP; ++sp)
             for (int j0 = o0[sp] + B_G * B_U + gl; j0 < o1[sp]; j0 += B_G * B_U)
-                push_b_chunk<STDP, STP>(D, j0, o1[sp], base[sp], lo_post, acc_s, lp_s, rel[sp], plastic[sp], t,
+                push_b_chunk<STDP, STP>(D, j0, o1[sp], base[sp], lo_post, acc_s, age_s, rel[sp], plastic[sp], t,
                                         lr);
     }
     if (D.sharded) {  // events = the rank's segments of the spikers' rows
@@ -740,7 +754,7 @@ struct EngineProp : snnb::Engine {
         int dev_sms = 0, smem_optin = 0;
         SNN_CUDA(cudaDeviceGetAttribute(&dev_sms, cudaDevAttrMultiProcessorCount, cfg.device));
         SNN_CUDA(cudaDeviceGetAttribute(&smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, cfg.device));
-        const int slot_bytes = stdp ? 8 : 4;  // int32 sum (+ int32 last post spike with STDP)
+        const int slot_bytes = stdp ? 6 : 4;  // int32 sum (+ the post's 16-bit spike age with STDP)
         const int bw_cap = std::max(1024, std::min(SNN_B_WMAX, smem_optin / slot_bytes));
         const int nb_min = (int)(((long long)N + bw_cap - 1) / bw_cap);
         sorted = nb_min <= 256 && F <= 65535;
@@ -783,7 +797,8 @@ struct EngineProp : snnb::Engine {
             }
             SNN_REQUIRE(!cands.empty(), SNN_ERR_CUDA, "no bucket width fits the bucketed push");
             for (const Cand& c : cands)
-                if (c.util >= best - 0.01) {
+                // (with STDP within 3 %: fewer, wider buckets for longer LTD segments)
+                if (c.util >= best - (stdp ? 0.03 : 0.01)) {
                     D.nb = c.nb;
                     D.bw = c.bw;
                     D.parts = c.parts;
