@@ -523,12 +523,18 @@ __global__ void __launch_bounds__(P_THREADS) k4_ltp(PDev D, int k) {
                     if (p < D.n_exc) tp[u] = pre_before(D, p, t);
                 }
             }
+            // all weight loads before any store: the synapses of one post's
+            // list are distinct, so the loads cannot see these stores, and
+            // the P_UNROLL random reads overlap instead of queueing behind
+            // each store
+            float wv[P_UNROLL];
+#pragma unroll
+            for (int u = 0; u < P_UNROLL; ++u) wv[u] = tp[u] >= 0 ? __ldcg(D.w + s[u]) : 0.0f;
 #pragma unroll
             for (int u = 0; u < P_UNROLL; ++u) {
                 if (tp[u] >= 0) {
                     const float dw = pm_mul(0.05f, e20(D, t - tp[u]));
-                    const float wv = __ldcg(D.w + s[u]);
-                    D.w[s[u]] = pm_min(pm_max(pm_fma(lr, dw, wv), 0.0f), D.w_max);
+                    D.w[s[u]] = pm_min(pm_max(pm_fma(lr, dw, wv[u]), 0.0f), D.w_max);
                 }
             }
         }
