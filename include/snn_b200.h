@@ -208,6 +208,30 @@ int snn_build_columns(snn_ctx* ctx, const snn_topology_spec* spec);
  * are copied to device memory. */
 int snn_set_corpus(snn_ctx* ctx, const uint8_t* bytes, int64_t n);
 
+/* snn_set_corpus with options.  flags = SNN_CORPUS_TEXT_FILTER applies the
+ * reference's text-corpus filter first: NUL bytes dropped, CR / LF / TAB
+ * mapped to a space, every other byte (UTF-8 included) kept
+ * (src/stage2e/input_encoding.cu:49-64, src/stage2/text_stream.cu:38-52);
+ * flags = 0 is snn_set_corpus.  n_kept (nullable) receives the length of the
+ * corpus the network reads. */
+#define SNN_CORPUS_TEXT_FILTER 1
+int snn_set_corpus_ex(snn_ctx* ctx, const uint8_t* bytes, int64_t n, int32_t flags,
+                      int64_t* n_kept);
+
+/* stage2e::load_text_corpus(const char* path) (src/stage2e/input_encoding.cu:
+ * 40-96) and TextStream::load_from_file (src/stage2/text_stream.cu:30-63):
+ * reads the whole file, applies the text-corpus filter and makes the result
+ * the corpus (read position 0).  SNN_ERR_IO if the file cannot be read or
+ * nothing is left after filtering (the reference returns 0 / false there).
+ * n_kept (nullable) receives the filtered length. */
+int snn_load_text_corpus(snn_ctx* ctx, const char* path, int64_t* n_kept);
+
+/* Byte classes of a buffer, as the reference's loader reports them
+ * (src/stage2e/input_encoding.cu:68-74): out[0] ASCII (< 0x80), out[1] UTF-8
+ * lead bytes (0xC0..0xF7), out[2] continuation bytes (0x80..0xBF); n_out >= 3.
+ * Host only. */
+int snn_byte_classes(const uint8_t* bytes, int64_t n, int64_t* out, int32_t n_out);
+
 /* One step.  `step` must equal the number of steps executed so far.
  * Stage 2e: on steps with step % 3 == 0 the byte is inject_byte if >= 0,
  *   else the next corpus byte (or (step/3)%256 without a corpus).

@@ -66,16 +66,20 @@ public:
     // E0 ablation (src/stage2e/scheduler.cuh:72, synapse_kernels.cuh:82)
     void set_e0_ablation(bool enable) { detail::check(snn_set_e0(h_.ctx, enable), h_.ctx, "snn_set_e0"); }
 
-    // load_text_corpus: returns the number of bytes loaded (0 on failure)
+    // load_text_corpus (src/stage2e/input_encoding.cu:40-96): the reference's
+    // filter is applied by the C ABI; returns the number of bytes kept
     size_t load_text_corpus(const std::vector<uint8_t>& bytes) {
-        std::vector<uint8_t> f;
-        f.reserve(bytes.size());
-        for (uint8_t c : bytes) {  // src/stage2e/input_encoding.cu:57-64
-            if (c == 0x00) continue;
-            f.push_back((c == '\r' || c == '\n' || c == '\t') ? (uint8_t)' ' : c);
-        }
-        detail::check(snn_set_corpus(h_.ctx, f.data(), (int64_t)f.size()), h_.ctx, "snn_set_corpus");
-        return f.size();
+        int64_t kept = 0;
+        detail::check(snn_set_corpus_ex(h_.ctx, bytes.data(), (int64_t)bytes.size(),
+                                        SNN_CORPUS_TEXT_FILTER, &kept),
+                      h_.ctx, "snn_set_corpus_ex");
+        return (size_t)kept;
+    }
+    // the same from a file path, as the reference's load_text_corpus(const char*)
+    size_t load_text_corpus(const char* path) {
+        int64_t kept = 0;
+        detail::check(snn_load_text_corpus(h_.ctx, path, &kept), h_.ctx, "snn_load_text_corpus");
+        return (size_t)kept;
     }
 
     void step(int current_step) { detail::check(snn_step(h_.ctx, current_step, -1, 1), h_.ctx, "snn_step"); }

@@ -12,10 +12,15 @@
 //       run (i32[N]), fire rates (f32[N]), alpha (f32[S]), beta (f32[S]),
 //       receptor flags (u8[S]) and the neuron x byte counts (i32[N*256]):
 //       the long-run statistics the tests compare with this library's engine.
-//   ref_run --steps K [--corpus F] --time W
+//   ref_run --steps K [--corpus F] --time W [--step0 T0]
 //       W untimed warm-up steps, then K timed steps of the reference's own
 //       host loop (src/stage2e/main.cpp:679-743, without CSV); prints
-//       REF_STEPS_PER_SEC and REF_EVENTS_PER_SEC.
+//       REF_STEPS_PER_SEC and REF_EVENTS_PER_SEC.  The scheduler is given
+//       the step numbers T0, T0 + 1, ... (default 0): its phase table is a
+//       function of the step number, so T0 = 5010 runs a fresh network in
+//       the SYNAPTOGENIC phase with the injection (t % 3) and the 10-step
+//       schedules aligned with steps 0, 1, ... of a network whose phase is
+//       offset by 5000.
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -37,7 +42,7 @@ static uint64_t fnv(const void* p, size_t n, uint64_t h = 1469598103934665603ull
 }
 
 int main(int argc, char** argv) {
-    int steps = 100, warm = -1;
+    int steps = 100, warm = -1, step0 = 0;
     const char* corpus = nullptr;
     const char* dump = nullptr;
     const char* state = nullptr;
@@ -49,6 +54,7 @@ int main(int argc, char** argv) {
         else if (!strcmp(argv[i], "--state") && i + 1 < argc) state = argv[++i];
         else if (!strcmp(argv[i], "--stats") && i + 1 < argc) stats = argv[++i];
         else if (!strcmp(argv[i], "--time") && i + 1 < argc) warm = atoi(argv[++i]);
+        else if (!strcmp(argv[i], "--step0") && i + 1 < argc) step0 = atoi(argv[++i]);
     }
     int dev_count = 0;
     if (cudaGetDeviceCount(&dev_count) != cudaSuccess || dev_count == 0) {
@@ -66,11 +72,11 @@ int main(int argc, char** argv) {
     stage2e::BioMechanismScheduler sched(&alloc);
     const int N = N_TOTAL_NEURONS_2E;
     if (warm >= 0) {
-        for (int s = 0; s < warm; ++s) sched.step(s);
+        for (int s = 0; s < warm; ++s) sched.step(step0 + s);
         cudaDeviceSynchronize();
         long long arr0 = sched.arrived_events_accum();
         auto t0 = std::chrono::steady_clock::now();
-        for (int s = warm; s < warm + steps; ++s) sched.step(s);
+        for (int s = warm; s < warm + steps; ++s) sched.step(step0 + s);
         cudaDeviceSynchronize();
         auto t1 = std::chrono::steady_clock::now();
         double sec = std::chrono::duration<double>(t1 - t0).count();

@@ -145,6 +145,57 @@ int snn_set_corpus(snn_ctx* ctx, const uint8_t* bytes, int64_t n) {
     return guard(ctx, [&] { ctx->eng->set_corpus(bytes, n); });
 }
 
+int snn_set_corpus_ex(snn_ctx* ctx, const uint8_t* bytes, int64_t n, int32_t flags,
+                      int64_t* n_kept) {
+    return guard(ctx, [&] {
+        SNN_REQUIRE(n >= 0 && (n == 0 || bytes), SNN_ERR_ARG, "bad corpus");
+        SNN_REQUIRE((flags & ~SNN_CORPUS_TEXT_FILTER) == 0, SNN_ERR_ARG, "unknown corpus flags");
+        if (!(flags & SNN_CORPUS_TEXT_FILTER)) {
+            ctx->eng->set_corpus(bytes, n);
+            if (n_kept) *n_kept = n;
+            return;
+        }
+        std::vector<uint8_t> kept((size_t)n);
+        const int64_t k = snnb::text_filter(bytes, n, kept.data());
+        ctx->eng->set_corpus(kept.data(), k);
+        if (n_kept) *n_kept = k;
+    });
+}
+
+int snn_load_text_corpus(snn_ctx* ctx, const char* path, int64_t* n_kept) {
+    return guard(ctx, [&] {
+        SNN_REQUIRE(path, SNN_ERR_ARG, "null path");
+        FILE* f = fopen(path, "rb");
+        SNN_REQUIRE(f, SNN_ERR_IO, std::string("cannot open ") + path);
+        std::vector<uint8_t> raw;
+        uint8_t buf[1 << 16];
+        size_t got;
+        while ((got = fread(buf, 1, sizeof(buf), f)) > 0) raw.insert(raw.end(), buf, buf + got);
+        const bool bad = ferror(f) != 0;
+        fclose(f);
+        SNN_REQUIRE(!bad, SNN_ERR_IO, std::string("read error on ") + path);
+        const int64_t k = snnb::text_filter(raw.data(), (int64_t)raw.size(), raw.data());
+        SNN_REQUIRE(k > 0, SNN_ERR_IO, std::string("no text left in ") + path);
+        ctx->eng->set_corpus(raw.data(), k);
+        if (n_kept) *n_kept = k;
+    });
+}
+
+int snn_byte_classes(const uint8_t* bytes, int64_t n, int64_t* out, int32_t n_out) {
+    if ((n > 0 && !bytes) || n < 0 || !out || n_out < 3) return SNN_ERR_ARG;
+    int64_t a = 0, h = 0, c = 0;
+    for (int64_t i = 0; i < n; ++i) {
+        const uint8_t b = bytes[i];
+        if (b < 0x80) ++a;
+        else if (b < 0xC0) ++c;
+        else if (b < 0xF8) ++h;
+    }
+    out[0] = a;
+    out[1] = h;
+    out[2] = c;
+    return SNN_OK;
+}
+
 int snn_step(snn_ctx* ctx, int32_t step, int32_t inject_byte, int32_t learn) {
     return guard(ctx, [&] {
         SNN_REQUIRE(step == ctx->eng->steps_done(), SNN_ERR_STATE,

@@ -30,6 +30,20 @@ struct Error : std::runtime_error {
         if (!(cond)) throw ::snnb::Error(code, msg); \
     } while (0)
 
+// The reference's text-corpus filter (src/stage2e/input_encoding.cu:49-64,
+// src/stage2/text_stream.cu:38-52): NUL dropped, CR / LF / TAB mapped to a
+// space, every other byte kept.  Writes the kept bytes to out (which may be
+// `in` itself) and returns their count.
+inline int64_t text_filter(const uint8_t* in, int64_t n, uint8_t* out) {
+    int64_t k = 0;
+    for (int64_t i = 0; i < n; ++i) {
+        const uint8_t c = in[i];
+        if (c == 0x00) continue;
+        out[k++] = (c == '\r' || c == '\n' || c == '\t') ? (uint8_t)' ' : c;
+    }
+    return k;
+}
+
 // Owning device allocation.
 template <typename T>
 struct DevBuf {

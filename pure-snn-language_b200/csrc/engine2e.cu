@@ -1698,19 +1698,24 @@ struct Engine2e : snnb::Engine {
                                          (double)h.ltp_visits);
     }
 
-    // Algorithmic HBM bytes of `n` steps under this layout:
-    // dense per step: group id 4*S + Ca read/write 8*S_exc; events: dispatch
-    // 16 (alpha,beta read; value write 4 + ring sector), arrival 24 (value
-    // read 4, alpha/beta/auto/elig read+write 32 shared with LTD), LTP 32.
+    // Algorithmic HBM bytes of the synapse pass over the first `n` steps
+    // (the traffic its semantics require under this layout): every step the
+    // group id of every synapse (4 B) and the Ca of every excitatory synapse
+    // (read + write, 8 B); per dispatched edge 12 B (alpha, beta read; value
+    // write); per arrival 36 B (value read; plasticity record read + write);
+    // per LTP visit 32 B (plasticity record read + write); every 10 steps
+    // eligibility (8 B) and e1 / e2 (16 B) of every synapse plus CaMKII act /
+    // autophosphorylation (16 B) of every excitatory one, read + write; every
+    // 1000 steps alpha / beta (16 B) of every synapse.
     double modeled_bytes(long long n, double arr, double disp, double ltp) const {
         double s_exc = 0;
         for (int64_t g = 0; g < lay.G; ++g)
             if (lay.gmeta[g] & GV_EXC) s_exc += lay.gsize[g];
         const double S = (double)net.S;
-        double dense = n * (4.0 * S + 8.0 * s_exc);
-        double periodic = (double)((n + 9) / 10) * (S * (16.0 + 8.0 + 8.0) + s_exc * 8.0) +
-                          (double)((n + 999) / 1000) * S * 16.0;
-        double events = disp * 12.0 + arr * (4.0 + 32.0) + ltp * 32.0;
+        const double dense = n * (4.0 * S + 8.0 * s_exc);
+        const double periodic = (double)((n + 9) / 10) * (24.0 * S + 16.0 * s_exc) +
+                                (double)((n + 999) / 1000) * 16.0 * S;
+        const double events = disp * 12.0 + arr * 36.0 + ltp * 32.0;
         return dense + periodic + events;
     }
 

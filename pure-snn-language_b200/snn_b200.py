@@ -25,6 +25,7 @@ ERRORS = {1: "SNN_ERR_ARG", 2: "SNN_ERR_CUDA", 3: "SNN_ERR_OOM", 4: "SNN_ERR_STA
 MODEL_STAGE2E, MODEL_STAGE0, MODEL_PROP = 0, 1, 2
 PROP_PLAIN, PROP_STDP, PROP_STP = 0, 1, 2
 PRESET_REF, PRESET_BASELINE = 0, 1
+CORPUS_TEXT_FILTER = 1
 FMT_NATIVE, FMT_SNN2_V1, FMT_SCKP_V2, FMT_RAW_F32 = 0, 1, 2, 3
 
 STATE = {
@@ -118,7 +119,8 @@ EXPORTS = ["snn_config_init", "snn_topology_init", "snn_create", "snn_destroy",
            "snn_run", "snn_synchronize", "snn_get_spikes", "snn_get_state", "snn_get_counters",
            "snn_set_dopamine", "snn_set_e0", "snn_save", "snn_load", "snn_stream_generate",
            "snn_set_profiling", "snn_get_profile", "snn_propagate", "snn_propagate_static",
-           "snn_nccl_unique_id", "snn_set_shard", "snn_shard_plan", "snn_semantic_eval"]
+           "snn_nccl_unique_id", "snn_set_shard", "snn_shard_plan", "snn_semantic_eval",
+           "snn_set_corpus_ex", "snn_load_text_corpus", "snn_byte_classes"]
 
 _lib = None
 
@@ -141,6 +143,9 @@ def lib():
         L.snn_version.restype = C.c_char_p
         L.snn_build_columns.argtypes = [vp, C.POINTER(TopologySpec)]
         L.snn_set_corpus.argtypes = [vp, vp, C.c_int64]
+        L.snn_set_corpus_ex.argtypes = [vp, vp, C.c_int64, C.c_int32, vp]
+        L.snn_load_text_corpus.argtypes = [vp, C.c_char_p, vp]
+        L.snn_byte_classes.argtypes = [vp, C.c_int64, vp, C.c_int32]
         L.snn_step.argtypes = [vp, C.c_int32, C.c_int32, C.c_int32]
         L.snn_run.argtypes = [vp, C.c_int32, vp, C.c_int64, C.c_int32, vp, vp]
         L.snn_synchronize.argtypes = [vp]
@@ -213,12 +218,16 @@ def stream(n, seed=42, p_cjk=0.452, zipf_s=1.1):
 
 
 def byte_classes(b):
-    """Fractions of ASCII, UTF-8 head and continuation bytes."""
-    b = np.asarray(b)
-    n = max(b.size, 1)
-    return {"ascii": float((b < 0x80).sum()) / n,
-            "head": float(((b >= 0xC0) & (b < 0xF8)).sum()) / n,
-            "continuation": float(((b >= 0x80) & (b < 0xC0)).sum()) / n}
+    """Fractions of ASCII (< 0x80), UTF-8 lead (0xC0..0xF7) and continuation
+    (0x80..0xBF) bytes (snn_byte_classes)."""
+    a = np.ascontiguousarray(np.frombuffer(bytes(b), np.uint8))
+    out = np.zeros(3, np.int64)
+    rc = lib().snn_byte_classes(a.ctypes.data, a.size, out.ctypes.data, 3)
+    if rc:
+        raise SnnError(rc, "snn_byte_classes")
+    n = max(a.size, 1)
+    return {"ascii": float(out[0]) / n, "head": float(out[1]) / n,
+            "continuation": float(out[2]) / n}
 
 
 def topology(model=MODEL_STAGE2E, n_columns=50, **overrides):
@@ -283,9 +292,23 @@ class Network:
         self.n_columns = spec.n_columns
         return self
 
-    def set_corpus(self, data):
+    def set_corpus(self, data, text_filter=False):
+        """The byte stream the network reads (one byte per inject step,
+        wrapping).  text_filter=True applies the reference's corpus filter
+        (NUL dropped, CR / LF / TAB -> space); returns the kept length."""
         b = np.ascontiguousarray(np.frombuffer(bytes(data), np.uint8))
-        self._check(self.L.snn_set_corpus(self.h, b.ctypes.data, b.size))
+        kept = C.c_int64(0)
+        self._check(self.L.snn_set_corpus_ex(self.h, b.ctypes.data, b.size,
+                                             CORPUS_TEXT_FILTER if text_filter else 0,
+                                             C.byref(kept)))
+        return kept.value
+
+    def load_text_corpus(self, path):
+        """Read a text file, filter it like the reference's load_text_corpus
+        and make it the corpus; returns the kept length."""
+        kept = C.c_int64(0)
+        self._check(self.L.snn_load_text_corpus(self.h, os.fsencode(path), C.byref(kept)))
+        return kept.value
 
     def step(self, step, inject_byte=-1, learn=True):
         self._check(self.L.snn_step(self.h, step, inject_byte, int(learn)))

@@ -4,7 +4,7 @@ src/stage2e/network_init.cu:158-473), compiled unmodified from the reference
 tree into oracle/_ref/topo_pin by oracle/ref/Makefile.  Run on the machine that
 has the reference tree:
 
-    make -C oracle/ref REF=/root/reference/src
+    make -C oracle/ref REF=<reference project>/src
     python tests/golden/make_topology_pin.py
 """
 import json
