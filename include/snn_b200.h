@@ -87,7 +87,10 @@ extern "C" {
 #define SNN_PROP_STDP 1
 #define SNN_PROP_STP 2
 
-#define SNN_PRESET_REF 0      /* constants exactly as the reference kernels */
+#define SNN_PRESET_REF 0      /* constants exactly as the reference kernels
+                                 (Stage 0 model: the reference's Stage 0 build
+                                 for the block network, its Stage 2 build for
+                                 columns) */
 #define SNN_PRESET_BASELINE 1 /* constants as stated in the benchmark spec  */
 
 typedef struct snn_ctx snn_ctx;
@@ -364,7 +367,10 @@ int snn_propagate(const int32_t* post, const float* w, int64_t n_pre, int32_t fa
  * snn_propagate; the spike list lives in a file-scope device array of
  * 1,048,576 entries (4 MiB), so n_pre above 1,048,576 is rejected with
  * SNN_ERR_ARG.  The first call on a device looks up that array's address
- * (with the device current), so make it before any stream capture.  Each
+ * (with the device current), so make it before any stream capture; the
+ * address is kept for the life of the process, so a device reset
+ * (cudaDeviceReset) or a new primary context invalidates it (as it does the
+ * scratch of snn_propagate): do not call either after one.  Each
  * call zeroes the list count on `stream` before use.  All calls on one device
  * share the array: calls that overlap in time on different streams race and
  * give wrong sums; order them on one stream (or with events). */

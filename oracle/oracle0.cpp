@@ -80,7 +80,9 @@ struct O0 {
     bool reset_pending = false;
 };
 
-void gen_topology(O0& o) {
+// neuron types and regions: the first 80 % of every region (Stage 0) or
+// layer of a column (Stage 2) are excitatory (src/include/types.h:173-205)
+void gen_layout(O0& o) {
     const O0Params& P = o.P;
     const int per = P.n_sens + P.n_assoc + P.n_motor;
     const int ncol = P.n_columns > 0 ? P.n_columns : 1;
@@ -96,6 +98,23 @@ void gen_topology(O0& o) {
         o.region[i] = (uint8_t)r;
         o.type[i] = lo < (int)pm_mul(pm_i2f(sz), 0.8f) ? 0 : 1;
     }
+}
+
+// incoming lists: every post's synapses in ascending synapse id
+void build_in_lists(O0& o) {
+    o.in_ptr.assign(o.N + 1, 0);
+    for (long long s = 0; s < o.S; ++s) o.in_ptr[o.post[s] + 1]++;
+    for (int i = 0; i < o.N; ++i) o.in_ptr[i + 1] += o.in_ptr[i];
+    o.in_syn.resize(o.S);
+    std::vector<int32_t> fill(o.in_ptr.begin(), o.in_ptr.end() - 1);
+    for (long long s = 0; s < o.S; ++s) o.in_syn[fill[o.post[s]]++] = (int32_t)s;
+}
+
+void gen_topology(O0& o) {
+    const O0Params& P = o.P;
+    gen_layout(o);
+    const int per = P.n_sens + P.n_assoc + P.n_motor;
+    const int ncol = P.n_columns > 0 ? P.n_columns : 1;
     SplitMix64 rng{P.seed};
     const int deg = P.deg_intra + (P.n_columns > 0 ? P.deg_inter : 0);
     o.S = (long long)o.N * deg;
@@ -125,16 +144,10 @@ void gen_topology(O0& o) {
             ++k;
         }
     }
-    o.in_ptr.assign(o.N + 1, 0);
-    for (long long s = 0; s < o.S; ++s) o.in_ptr[o.post[s] + 1]++;
-    for (int i = 0; i < o.N; ++i) o.in_ptr[i + 1] += o.in_ptr[i];
-    o.in_syn.resize(o.S);
-    std::vector<int32_t> fill(o.in_ptr.begin(), o.in_ptr.end() - 1);
-    for (long long s = 0; s < o.S; ++s) o.in_syn[fill[o.post[s]]++] = (int32_t)s;
+    build_in_lists(o);
 }
 
-void setup(O0& o) {
-    gen_topology(o);
+void init_state(O0& o) {
     const int N = o.N;
     o.V.assign(N, 0.0f); o.I.assign(N, 0.0f); o.fr.assign(N, 0.0f);
     o.ref.assign(N, 0); o.last_lif.assign(N, -1000); o.off.assign(N, 0);
@@ -262,7 +275,31 @@ extern "C" {
 void* o0_create(const O0Params* p) {
     O0* o = new O0();
     o->P = *p;
-    setup(*o);
+    gen_topology(*o);
+    init_state(*o);
+    return o;
+}
+// the network of an explicit synapse list (e.g. a topology the reference
+// generated): synapse s runs pre[s] -> post[s] with weight w[s]; every post's
+// incoming synapses are propagated in ascending s.  Returns null when the
+// list does not fit the layout of p.
+void* o0_create_synapses(const O0Params* p, int64_t S, const int32_t* pre, const int32_t* post,
+                         const float* w) {
+    O0* o = new O0();
+    o->P = *p;
+    gen_layout(*o);
+    o->S = S;
+    o->pre.assign(pre, pre + S);
+    o->post.assign(post, post + S);
+    o->w.assign(w, w + S);
+    o->elig.assign(S, 0.0f);
+    for (int64_t s = 0; s < S; ++s)
+        if (pre[s] < 0 || pre[s] >= o->N || post[s] < 0 || post[s] >= o->N) {
+            delete o;
+            return nullptr;
+        }
+    build_in_lists(*o);
+    init_state(*o);
     return o;
 }
 void o0_destroy(void* h) { delete (O0*)h; }

@@ -21,12 +21,25 @@
 //       untimed steps reading the spike flags back each step to count the
 //       events (out-edges of spiking neurons, from the CSR's column indices).
 //       Prints REF_STEPS_PER_SEC, REF_EVENTS_PER_STEP, REF_EVENTS_PER_SEC.
+//
+//   ref_run0 --dump DIR --steps K
+//       Pinning fixtures of the reference's own deterministic step (fixed
+//       256-wide shared-memory tree in the propagation, one thread per
+//       synapse in the STDP): DIR/net.snn2, the freshly initialised network
+//       in the reference's SNN2 v1 checkpoint layout
+//       (src/stage2/unsupervised_trainer.cu:176-262: header, Synapse records,
+//       row_ptr, col_idx, weights); DIR/bytes.bin, the K input bytes;
+//       DIR/spikes.txt, one line per step "t count fnv64(spiking indices)";
+//       after the K steps DIR/final_V.bin, final_I.bin, final_fr.bin
+//       (float[N]), final_off.bin (int8[N] threshold offsets) and
+//       final_w.bin (float[S], d_weights in CSR order).
 #include <chrono>
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <vector>
+#include <string>
 #include <cuda_runtime.h>
 #include "config.h"
 #include "types.h"
@@ -35,11 +48,27 @@
 #include "columnar_topology.cuh"
 #endif
 
+static uint64_t fnv64(const void* p, size_t n) {
+    uint64_t h = 1469598103934665603ull;
+    const unsigned char* b = (const unsigned char*)p;
+    for (size_t i = 0; i < n; ++i) { h ^= b[i]; h *= 1099511628211ull; }
+    return h;
+}
+
+static bool write_file(const std::string& path, const void* p, size_t n) {
+    FILE* f = fopen(path.c_str(), "wb");
+    if (!f) return false;
+    const bool ok = fwrite(p, 1, n, f) == n;
+    return fclose(f) == 0 && ok;
+}
+
 int main(int argc, char** argv) {
     int steps = 1000, warm = 100;
+    const char* dump = nullptr;
     for (int i = 1; i < argc; ++i) {
         if (!strcmp(argv[i], "--steps") && i + 1 < argc) steps = atoi(argv[++i]);
         else if (!strcmp(argv[i], "--time") && i + 1 < argc) warm = atoi(argv[++i]);
+        else if (!strcmp(argv[i], "--dump") && i + 1 < argc) dump = argv[++i];
     }
     int dev_count = 0;
     if (cudaGetDeviceCount(&dev_count) != cudaSuccess || dev_count == 0) {
@@ -83,6 +112,74 @@ int main(int argc, char** argv) {
         buf[prev] = in_val;
         net.step(buf.data(), t);
     };
+    if (dump) {
+        const std::string dir(dump);
+        std::vector<unsigned char> file;
+        auto put = [&](const void* p, size_t n) {
+            const unsigned char* b = (const unsigned char*)p;
+            file.insert(file.end(), b, b + n);
+        };
+        const uint32_t magic = 0x534E4E32u, version = 1u;
+        const int64_t step0 = 0;
+        const uint64_t pos0 = 0;
+        const int32_t nn = N, ns = S;
+        put(&magic, 4); put(&version, 4); put(&step0, 8); put(&pos0, 8); put(&nn, 4); put(&ns, 4);
+        std::vector<Synapse> syn((size_t)S);
+        std::vector<int> rp((size_t)N + 1);
+        std::vector<float> wts((size_t)S);
+        cudaMemcpy(syn.data(), net.get_d_synapses(), (size_t)S * sizeof(Synapse), cudaMemcpyDeviceToHost);
+        cudaMemcpy(rp.data(), net.get_d_row_ptr(), ((size_t)N + 1) * 4, cudaMemcpyDeviceToHost);
+        cudaMemcpy(wts.data(), net.get_d_weights(), (size_t)S * 4, cudaMemcpyDeviceToHost);
+        put(syn.data(), (size_t)S * sizeof(Synapse));
+        put(rp.data(), ((size_t)N + 1) * 4);
+        put(col.data(), (size_t)S * 4);
+        put(wts.data(), (size_t)S * 4);
+        if (!write_file(dir + "/net.snn2", file.data(), file.size())) {
+            fprintf(stderr, "ref_run0: cannot write %s/net.snn2\n", dump);
+            return 3;
+        }
+        std::vector<unsigned char> bytes;
+        std::vector<unsigned char> sp((size_t)N);
+        std::vector<int> idx;
+        FILE* fs = fopen((dir + "/spikes.txt").c_str(), "w");
+        if (!fs) return 3;
+        for (int t = 0; t < steps; ++t) {
+            one_step(t);
+            bytes.push_back((unsigned char)prev);
+            cudaMemcpy(sp.data(), net.get_d_spikes(), (size_t)N, cudaMemcpyDeviceToHost);
+            idx.clear();
+            for (int j = 0; j < N; ++j)
+                if (sp[j]) idx.push_back(j);
+            fprintf(fs, "%d %zu %llu\n", t, idx.size(),
+                    (unsigned long long)fnv64(idx.data(), idx.size() * 4));
+        }
+        fclose(fs);
+        std::vector<NeuronState> neu((size_t)N);
+        cudaMemcpy(neu.data(), net.get_d_neurons(), (size_t)N * sizeof(NeuronState), cudaMemcpyDeviceToHost);
+        cudaMemcpy(wts.data(), net.get_d_weights(), (size_t)S * 4, cudaMemcpyDeviceToHost);
+        std::vector<float> V((size_t)N), I((size_t)N), fr((size_t)N);
+        std::vector<signed char> off((size_t)N);
+        for (int j = 0; j < N; ++j) {
+            V[j] = neu[j].membrane_potential;
+            I[j] = neu[j].synaptic_current;
+            fr[j] = neu[j].fire_rate;
+            off[j] = neu[j].threshold_offset;
+        }
+        const cudaError_t err = cudaGetLastError();
+        if (err != cudaSuccess) {
+            fprintf(stderr, "ref_run0: %s\n", cudaGetErrorString(err));
+            return 5;
+        }
+        bool ok = write_file(dir + "/bytes.bin", bytes.data(), bytes.size()) &&
+                  write_file(dir + "/final_V.bin", V.data(), (size_t)N * 4) &&
+                  write_file(dir + "/final_I.bin", I.data(), (size_t)N * 4) &&
+                  write_file(dir + "/final_fr.bin", fr.data(), (size_t)N * 4) &&
+                  write_file(dir + "/final_off.bin", off.data(), (size_t)N) &&
+                  write_file(dir + "/final_w.bin", wts.data(), (size_t)S * 4);
+        if (!ok) return 3;
+        printf("REF_DUMP %d steps N %d S %d\n", steps, N, S);
+        return 0;
+    }
     int t = 0;
     for (; t < warm; ++t) one_step(t);
     cudaDeviceSynchronize();

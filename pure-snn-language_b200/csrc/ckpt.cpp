@@ -113,7 +113,16 @@ void load_native(const char* path, int32_t model, void* blob, uint32_t blob_byte
         const uint64_t nb = f.get_v<uint64_t>();
         SNN_REQUIRE(strncmp(name, s.name, NAME_BYTES) == 0 && nb == (uint64_t)s.bytes, SNN_ERR_IO,
                     std::string("checkpoint section differs at ") + s.name);
-        f.seek(f.tell() + (long long)nb);
+        if (s.validate) {
+            std::vector<char> buf(std::min((size_t)nb, CHUNK));
+            for (size_t off = 0; off < nb; off += CHUNK) {
+                const size_t m = std::min(CHUNK, (size_t)nb - off);
+                f.get(buf.data(), m);
+                s.validate(buf.data(), m, off);
+            }
+        } else {
+            f.seek(f.tell() + (long long)nb);
+        }
     }
     if (check) check(hb.data());
     f.seek(first);

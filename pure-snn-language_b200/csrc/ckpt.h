@@ -47,6 +47,10 @@ struct DevSection {
     const char* name;
     void* dev;
     size_t bytes;
+    // optional: sees the file's data of the section, in chunks (offset in
+    // bytes from its start), before anything reaches the device; throws to
+    // refuse the file
+    std::function<void(const char*, size_t, size_t)> validate = nullptr;
 };
 
 void save_native(const char* path, int32_t model, const void* blob, uint32_t blob_bytes,

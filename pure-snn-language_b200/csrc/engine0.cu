@@ -193,6 +193,25 @@ __global__ void __launch_bounds__(256) k0_stdp(Dev d, Consts k, int kstep) {
         const unsigned p = pp & 0x7fffffffu;
         const bool inh = pp >> 31;
         const bool pf = snow[p];
+#ifdef SNN_REFMATH
+        // the reference's expressions as written (CUDA expf, the compiler's
+        // default contraction), for agreement with the reference binary
+        float delta_w = 0.0f;
+        if (pf) {
+            const float dt = LSq - tf;
+            if (dt < 0.0f && LSq > -500.0f) delta_w -= 0.05f * expf(dt / 20.0f);
+        }
+        if (qf) {
+            const float LSp = pf ? d.B[p] : d.A[p];
+            const float dt = tf - LSp;
+            if (dt > 0.0f && LSp > -500.0f) delta_w += 0.05f * expf(-dt / 20.0f);
+        }
+        const float el = 0.95f * d.e[i] + delta_w;
+        d.e[i] = el;
+        const float weight_delta = da * el;
+        float w = d.w[i];
+        w += weight_delta;
+#else
         float dw = 0.0f;
         if (pf) {
             const float dt = pm_sub(LSq, tf);
@@ -206,6 +225,7 @@ __global__ void __launch_bounds__(256) k0_stdp(Dev d, Consts k, int kstep) {
         const float el = pm_fma(k.elig_decay, d.e[i], dw);
         d.e[i] = el;
         float w = pm_fma(da, el, d.w[i]);
+#endif
         if (!inh) { if (w > k.w_max) w = k.w_max; if (w < 0.0f) w = 0.0f; }
         else { if (w > 0.0f) w = 0.0f; if (w < -k.w_max) w = -k.w_max; }
         d.w[i] = w;
@@ -276,9 +296,20 @@ struct Engine0 : snnb::Engine {
         // LIF / STDP constants (src/include/config.h:16-41)
         K.beta = 0.95f; K.thr = 1.0f; K.refr = 2; K.a_plus = 0.05f; K.a_minus = 0.05f;
         K.elig_decay = 0.95f; K.w_max = 1.0f; K.fr_decay = 0.95f;
+    }
+
+    // homeostasis and input drive: the benchmark's constants, or those of the
+    // reference's own build of the layout (block network = Stage 0 build,
+    // columns = Stage 2 build)
+    void set_preset_consts(bool columnar) {
         if (cfg.preset == SNN_PRESET_BASELINE) {
             // benchmark configuration: I_ext 1.5, homeostatic LR 1e-4, 5 / 30 Hz targets
             K.in_gain = 1.5f; K.homeo_lr = 1e-4f; K.homeo_max = 2.0f;
+            K.target_sa = 0.005f; K.target_m = 0.030f;
+        } else if (!columnar) {
+            // Stage 0 build of the reference (src/include/config.h:33-40):
+            // LR 0.05, max offset 2.0, 5 / 30 Hz; one-hot drive 1.5
+            K.in_gain = 1.5f; K.homeo_lr = 0.05f; K.homeo_max = 2.0f;
             K.target_sa = 0.005f; K.target_m = 0.030f;
         } else {
             // Stage 2 build of the reference (src/include/config.h:74-83,
@@ -300,6 +331,7 @@ struct Engine0 : snnb::Engine {
         SNN_REQUIRE(sp.l4 > 0 && sp.l23 > 0 && sp.l5 > 0 && sp.deg_intra > 0, SNN_ERR_ARG,
                     "stage0 topology: sensory / association / motor sizes and degree needed");
         ncol = sp.n_columns;
+        set_preset_consts(ncol > 0);
         per = sp.l4 + sp.l23 + sp.l5;
         N = (ncol > 0 ? ncol : 1) * per;
         SNN_REQUIRE(ncol != 1, SNN_ERR_ARG, "columnar stage0 needs >= 2 columns");

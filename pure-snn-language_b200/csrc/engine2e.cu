@@ -158,6 +158,34 @@ struct Dev {
     const int* gmir;        // mirror pre of each mirror group
 };
 
+// Exponentials on the simulation path.  The canonical build uses snn_expf
+// (shared bit for bit with the CPU oracle); the refmath build
+// (-DSNN_REFMATH, compiled with the compiler's default contraction) uses CUDA's
+// expf as the reference's kernels do, for agreement with the reference binary
+// instead of with the oracle.
+#ifdef SNN_REFMATH
+__device__ __forceinline__ float k_exp(float x) { return expf(x); }
+__global__ void k_exp_one(float x, float* out) { *out = expf(x); }
+#else
+__device__ __forceinline__ float k_exp(float x) { return snn_expf(x); }
+#endif
+
+// a constant decay exp(x), computed like the kernels compute theirs
+inline float const_exp(float x) {
+#ifdef SNN_REFMATH
+    float* d = nullptr;
+    float h = 0.0f;
+    SNN_CUDA(cudaMalloc((void**)&d, sizeof(float)));
+    k_exp_one<<<1, 1>>>(x, d);
+    const cudaError_t e = cudaMemcpy(&h, d, sizeof(float), cudaMemcpyDeviceToHost);
+    cudaFree(d);
+    SNN_CUDA(e);
+    return h;
+#else
+    return snn_expf(x);
+#endif
+}
+
 __device__ __forceinline__ int phase_of(long long step) {
     return step < 5000 ? 0 : step < 200000 ? 1 : step < 800000 ? 2 : step < 1500000 ? 3 : 4;
 }
@@ -214,7 +242,7 @@ __device__ void publish_step(const Dev& d, const Consts& k, const StepIn& s) {
         z = pm_fma(k.rec_ach, c1, z);
         z = pm_fma(k.rec_ne, c2, z);
         z = pm_fma(k.rec_ht5, c3, z);
-        M[e] = pm_div(1.0f, pm_add(1.0f, snn_expf(-z)));
+        M[e] = pm_div(1.0f, pm_add(1.0f, k_exp(-z)));
     }
     c->t = s.t;
     c->gain = learn ? c_phase_gain[ph] : 0.0f;
@@ -497,7 +525,7 @@ __global__ void __launch_bounds__(NEU_BLOCK) k_neurons(Dev d, Consts k) {
             float ea = pm_div(pm_sub(V, k.vt), k.dT);
             if (ea > 10.0f) ea = 10.0f;
             if (ea < -10.0f) ea = -10.0f;
-            const float et = pm_mul(k.dT, snn_expf(ea));
+            const float et = pm_mul(k.dT, k_exp(ea));
             const float dV = pm_mul(pm_add(pm_sub(pm_add(-V, et), w), I), k.inv_taum);
             const float dw = pm_mul(pm_fma(k.a_ad, V, -w), k.inv_tauw);
             V = pm_add(V, dV);
@@ -533,7 +561,7 @@ __global__ void __launch_bounds__(NEU_BLOCK) k_neurons(Dev d, Consts k) {
         }
         // Mg block and post trace of neuron i for this step's synapse pass
         const float Vb = pm_fma(50.0f, V, -70.0f);
-        const float e = snn_expf(pm_div(-Vb, 16.13f));
+        const float e = k_exp(pm_div(-Vb, 16.13f));
         d.mg[i] = pm_div(1.0f, pm_add(1.0f, pm_div(pm_mul(1.0f, e), 3.57f)));
         float xp = pm_mul(nu.xpost, k.dec_xpost);
         if (spike) xp = pm_add(xp, k.a_minus);
@@ -1186,31 +1214,31 @@ struct Engine2e : snnb::Engine {
         k.fr_refr = 0.99f; k.fr_spk_keep = 0.9f; k.fr_spk_add = 0.1f; k.fr_quiet = 0.995f;
         k.off_decay = 0.999f; k.refr_steps = 2;
         k.off_add = (int)pm_mul(0.001f, 256.0f); k.off_max = (int)pm_mul(0.3f, 256.0f);
-        k.dec_nmda = snn_expf(pm_div(-1.0f, 150.0f));
-        k.dec_ampa = snn_expf(pm_div(-1.0f, 5.0f));
-        k.dec_ca = snn_expf(pm_div(-1.0f, 50.0f));
-        k.dec_ca_ff = snn_expf(pm_div(-1.0f, 10.0f));
+        k.dec_nmda = const_exp(pm_div(-1.0f, 150.0f));
+        k.dec_ampa = const_exp(pm_div(-1.0f, 5.0f));
+        k.dec_ca = const_exp(pm_div(-1.0f, 50.0f));
+        k.dec_ca_ff = const_exp(pm_div(-1.0f, 10.0f));
         k.ca_max = 1.0f; k.ca_max_ff = 0.12f;
-        k.rec_ff_step = pm_sub(1.0f, snn_expf(pm_div(-1.0f, 3.0f)));
-        k.dec_xpre = snn_expf(pm_div(-1.0f, 20.0f));
-        k.dec_xpost = snn_expf(pm_div(-1.0f, 20.0f));
+        k.rec_ff_step = pm_sub(1.0f, const_exp(pm_div(-1.0f, 3.0f)));
+        k.dec_xpre = const_exp(pm_div(-1.0f, 20.0f));
+        k.dec_xpost = const_exp(pm_div(-1.0f, 20.0f));
         k.g_nmda = 0.5f; k.ca_gain = 1000.0f; k.e_rev = 1.4f; k.i_gain = 0.05f; k.i_min = 1e-6f;
         const float taus_f[NCLASS] = {200.0f, 200.0f, 200.0f}, taus_r[NCLASS] = {3.0f, 500.0f, 500.0f};
         const float Us[NCLASS] = {0.02f, 0.2f, 0.05f};
         for (int q = 0; q < NCLASS; ++q) {
             k.U[q] = Us[q];
-            k.fac[q] = snn_expf(pm_div(-1.0f, taus_f[q]));
-            k.rec[q] = pm_sub(1.0f, snn_expf(pm_div(-1.0f, taus_r[q])));
+            k.fac[q] = const_exp(pm_div(-1.0f, taus_f[q]));
+            k.rec[q] = pm_sub(1.0f, const_exp(pm_div(-1.0f, taus_r[q])));
         }
         k.a_plus = 0.03f; k.a_minus = 0.03f; k.w_max = 1.5f; k.eta = 20.0f; k.eta_ff = 2.0f;
         k.reb_thr = 0.15f; k.reb_gain = 0.5f; k.ab_min = 1e-4f; k.ab_reset = 0.05f; k.psw_decay = 0.95f;
-        k.e1_dec = snn_expf(pm_div(-10.0f, 20.0f));
-        k.e2_dec = snn_expf(pm_div(-10.0f, 200.0f));
+        k.e1_dec = const_exp(pm_div(-10.0f, 20.0f));
+        k.e2_dec = const_exp(pm_div(-10.0f, 200.0f));
         k.ck_k1 = 0.8f; k.ck_k2 = 0.1f; k.ck_k3 = 0.5f; k.ck_k4 = 0.05f; k.ck_pp1 = 0.5f; k.ck_dt = 10.0f;
-        k.mod_dec[0] = snn_expf(pm_div(-100.0f, 100.0f));
-        k.mod_dec[1] = snn_expf(pm_div(-100.0f, 200.0f));
-        k.mod_dec[2] = snn_expf(pm_div(-100.0f, 150.0f));
-        k.mod_dec[3] = snn_expf(pm_div(-100.0f, 300.0f));
+        k.mod_dec[0] = const_exp(pm_div(-100.0f, 100.0f));
+        k.mod_dec[1] = const_exp(pm_div(-100.0f, 200.0f));
+        k.mod_dec[2] = const_exp(pm_div(-100.0f, 150.0f));
+        k.mod_dec[3] = const_exp(pm_div(-100.0f, 300.0f));
         k.rec_da[0] = -0.3f; k.rec_da[1] = 0.5f;  // [0] inhibitory pre, [1] excitatory pre
         k.rec_ach = 0.3f;
         k.rec_ne = pm_div(pm_u2f((unsigned)pm_mul(0.3f, 127.0f)), 127.0f);
@@ -1227,8 +1255,8 @@ struct Engine2e : snnb::Engine {
             k.vt = 0.8f; k.dT = 0.08f; k.a_ad = 0.2f; k.b_ad = 0.32f;
             for (int q = 0; q < NCLASS; ++q) {
                 k.U[q] = 0.5f;
-                k.fac[q] = snn_expf(pm_div(-1.0f, 50.0f));
-                k.rec[q] = pm_sub(1.0f, snn_expf(pm_div(-1.0f, 200.0f)));
+                k.fac[q] = const_exp(pm_div(-1.0f, 50.0f));
+                k.rec[q] = pm_sub(1.0f, const_exp(pm_div(-1.0f, 200.0f)));
             }
             k.rec_ff_step = k.rec[0];
         }

@@ -72,6 +72,7 @@ struct PDev {
     // post range of this rank: buckets [b0, b0 + nb_loc), neurons [lo, hi)
     // (one GPU: the whole network); `sharded` counts events per local segment
     int b0, nb_loc, lo, hi, sharded;
+    int ltp_chunks;           // LTP work items per spiking post (LTP_CHUNK incoming synapses each)
 };
 
 __device__ __forceinline__ float e20(const PDev& D, int dt) {
@@ -95,7 +96,7 @@ __device__ __forceinline__ float ltd(const PDev& D, float w, int q, int t, float
 // exp(-dt/20) is 0 and the weight, which lies in [0, w_max], stays as it is)
 constexpr unsigned SNN_PROP_AGE_NONE = 0xFFFFu;
 __device__ __forceinline__ float ltd_age(const PDev& D, float w, unsigned age, float lr) {
-    if (age > SNN_PROP_EXP_STEPS) return w;
+    if (age > SNN_PROP_EXP_STEPS) return w;  // loaded weights are checked to lie in [0, w_max]
     const float dw = pm_mul(-0.05f, __ldg(D.exp_tab + age));
     return pm_min(pm_max(pm_fma(lr, dw, w), 0.0f), D.w_max);
 }
@@ -496,6 +497,11 @@ __device__ __forceinline__ int pre_before(const PDev& D, int p, int t) {
     return a < t ? a : __ldcg(D.tB + p);
 }
 
+// LTP of the excitatory incoming synapses of every LIF spike: one warp per
+// (spiking post, chunk of LTP_CHUNK incoming synapses), so that a few
+// thousand spiking posts still give enough warps to cover the latency of
+// the scattered weight updates (every synapse is updated once)
+constexpr uint32_t LTP_CHUNK = 256;
 __global__ void __launch_bounds__(P_THREADS) k4_ltp(PDev D, int k) {
     PCtrl* C = D.ctrl;
     if (!C->learn) return;
@@ -506,9 +512,15 @@ __global__ void __launch_bounds__(P_THREADS) k4_ltp(PDev D, int k) {
     const long long gw = ((long long)blockIdx.x * P_THREADS + threadIdx.x) >> 5;
     const long long nw = ((long long)gridDim.x * P_THREADS) >> 5;
     const uint32_t F = (uint32_t)D.F;
-    for (long long e = gw; e < (long long)n; e += nw) {
+    const int CH = D.ltp_chunks;
+    for (long long v = gw; v < (long long)n * CH; v += nw) {
+        const long long e = v / CH;
+        const uint32_t c = (uint32_t)(v - e * CH);
         const int j = D.post_list[e];
-        const uint32_t b = D.in_ptr[j], en = D.in_ptr[j + 1];
+        const uint32_t rb = D.in_ptr[j], re = D.in_ptr[j + 1];
+        const uint32_t b = rb + c * LTP_CHUNK;
+        if (b >= re) continue;
+        const uint32_t en = min(re, b + LTP_CHUNK);
         if (lane == 0) atomicAdd(&C->ltp_visits, (unsigned long long)(en - b));
         for (uint32_t x0 = b; x0 < en; x0 += 32 * P_UNROLL) {
             uint32_t s[P_UNROLL];
@@ -884,6 +896,8 @@ struct EngineProp : snnb::Engine {
         D.un_list = un_list.p; D.rn_list = rn_list.p;
         D.post_list = post_list.p; D.raster = raster.p; D.exp_tab = exp_tab.p; D.ctrl = ctrl.p;
         D.boff = boff.p;
+        D.ltp_chunks = (int)((max_in + LTP_CHUNK - 1) / LTP_CHUNK);
+        if (D.ltp_chunks < 1) D.ltp_chunks = 1;
         if (bucketed) {
             part.alloc((size_t)D.parts * N);
             part.zero(stream);
@@ -1212,7 +1226,24 @@ struct EngineProp : snnb::Engine {
         SNN_REQUIRE(world == 1, SNN_ERR_UNSUPPORTED, "a sharded microbench has no checkpoint format");
         const NativeBlob want = blob();
         NativeBlob got{};
-        snnb::load_native(path, SNN_MODEL_PROP, &got, sizeof(got), native_sections(), stream,
+        // the weights must keep their sign ranges (excitatory rows [0, w_max],
+        // inhibitory rows [-w_max, 0]): the push's int32 sums and the
+        // plasticity clamps rely on them
+        auto secs = native_sections();
+        const size_t n_exc_w = (size_t)D.n_exc * (size_t)D.F;
+        const float wm = D.w_max;
+        for (auto& sec : secs)
+            if (!strcmp(sec.name, "w"))
+                sec.validate = [n_exc_w, wm](const char* data, size_t n, size_t off) {
+                    const size_t i0 = off / sizeof(float), cnt = n / sizeof(float);
+                    const float* x = reinterpret_cast<const float*>(data);
+                    for (size_t q = 0; q < cnt; ++q) {
+                        const float v = x[q];
+                        const bool ok = (i0 + q < n_exc_w) ? (v >= 0.0f && v <= wm) : (v <= 0.0f && v >= -wm);
+                        SNN_REQUIRE(ok, SNN_ERR_IO, "checkpoint weight outside its range [0, w_max] / [-w_max, 0]");
+                    }
+                };
+        snnb::load_native(path, SNN_MODEL_PROP, &got, sizeof(got), secs, stream,
                           [&](const void* p) {
                               NativeBlob f;
                               memcpy(&f, p, sizeof(f));

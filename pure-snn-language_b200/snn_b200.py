@@ -18,6 +18,9 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libsnn_b200.so")
+# the same core built with the reference's arithmetic (CUDA expf, compiler
+# contraction of plain expressions) instead of the canonical one
+REFMATH_LIB_PATH = os.path.join(HERE, "libsnn_b200_refmath.so")
 
 SNN_OK = 0
 ERRORS = {1: "SNN_ERR_ARG", 2: "SNN_ERR_CUDA", 3: "SNN_ERR_OOM", 4: "SNN_ERR_STATE",
@@ -123,50 +126,60 @@ EXPORTS = ["snn_config_init", "snn_topology_init", "snn_create", "snn_destroy",
            "snn_set_corpus_ex", "snn_load_text_corpus", "snn_byte_classes"]
 
 _lib = None
+_lib_refmath = None
 
 
-def lib():
-    """Load libsnn_b200.so (raises if it was not built)."""
-    global _lib
+def lib(refmath=False):
+    """Load libsnn_b200.so, or with refmath=True libsnn_b200_refmath.so
+    (raises if it was not built)."""
+    global _lib, _lib_refmath
+    if refmath:
+        if _lib_refmath is None:
+            _lib_refmath = _load(REFMATH_LIB_PATH)
+        return _lib_refmath
     if _lib is None:
-        if not os.path.exists(LIB_PATH):
-            raise OSError(f"{LIB_PATH} is missing: build it with `make -C {HERE}`")
-        L = C.CDLL(LIB_PATH)
-        vp = C.c_void_p
-        L.snn_config_init.argtypes = [C.POINTER(Config), C.c_int32, C.c_int32]
-        L.snn_topology_init.argtypes = [C.POINTER(TopologySpec), C.c_int32, C.c_int32]
-        L.snn_create.argtypes = [C.POINTER(Config), C.POINTER(vp)]
-        L.snn_destroy.argtypes = [vp]
-        L.snn_destroy.restype = None
-        L.snn_last_error.argtypes = [vp]
-        L.snn_last_error.restype = C.c_char_p
-        L.snn_version.restype = C.c_char_p
-        L.snn_build_columns.argtypes = [vp, C.POINTER(TopologySpec)]
-        L.snn_set_corpus.argtypes = [vp, vp, C.c_int64]
-        L.snn_set_corpus_ex.argtypes = [vp, vp, C.c_int64, C.c_int32, vp]
-        L.snn_load_text_corpus.argtypes = [vp, C.c_char_p, vp]
-        L.snn_byte_classes.argtypes = [vp, C.c_int64, vp, C.c_int32]
-        L.snn_step.argtypes = [vp, C.c_int32, C.c_int32, C.c_int32]
-        L.snn_run.argtypes = [vp, C.c_int32, vp, C.c_int64, C.c_int32, vp, vp]
-        L.snn_synchronize.argtypes = [vp]
-        L.snn_get_spikes.argtypes = [vp, vp, C.c_int64]
-        L.snn_get_state.argtypes = [vp, C.c_int32, vp, C.c_int64]
-        L.snn_get_counters.argtypes = [vp, C.POINTER(Counters)]
-        L.snn_semantic_eval.argtypes = [vp, C.c_int64, C.POINTER(Semantic), vp, C.c_int64]
-        L.snn_set_dopamine.argtypes = [vp, C.c_float]
-        L.snn_set_e0.argtypes = [vp, C.c_int32]
-        L.snn_save.argtypes = [vp, C.c_char_p, C.c_int32]
-        L.snn_load.argtypes = [vp, C.c_char_p, C.c_int32]
-        L.snn_stream_generate.argtypes = [vp, C.c_int64, C.c_uint64, C.c_double, C.c_double]
-        L.snn_set_profiling.argtypes = [vp, C.c_int32]
-        L.snn_get_profile.argtypes = [vp, C.POINTER(Profile)]
-        L.snn_propagate.argtypes = [vp, vp, C.c_int64, C.c_int32, vp, vp, C.c_int64, C.c_int32, vp]
-        L.snn_propagate_static.argtypes = L.snn_propagate.argtypes
-        L.snn_nccl_unique_id.argtypes = [vp, C.c_int64]
-        L.snn_set_shard.argtypes = [vp, C.c_int32, C.c_int32, vp, C.c_int64]
-        L.snn_shard_plan.argtypes = [C.POINTER(TopologySpec), C.c_int32, C.c_int32, vp, C.c_int32]
-        _lib = L
+        _lib = _load(LIB_PATH)
     return _lib
+
+
+def _load(path):
+    if not os.path.exists(path):
+        raise OSError(f"{path} is missing: build it with `make -C {HERE}`")
+    L = C.CDLL(path)
+    vp = C.c_void_p
+    L.snn_config_init.argtypes = [C.POINTER(Config), C.c_int32, C.c_int32]
+    L.snn_topology_init.argtypes = [C.POINTER(TopologySpec), C.c_int32, C.c_int32]
+    L.snn_create.argtypes = [C.POINTER(Config), C.POINTER(vp)]
+    L.snn_destroy.argtypes = [vp]
+    L.snn_destroy.restype = None
+    L.snn_last_error.argtypes = [vp]
+    L.snn_last_error.restype = C.c_char_p
+    L.snn_version.restype = C.c_char_p
+    L.snn_build_columns.argtypes = [vp, C.POINTER(TopologySpec)]
+    L.snn_set_corpus.argtypes = [vp, vp, C.c_int64]
+    L.snn_set_corpus_ex.argtypes = [vp, vp, C.c_int64, C.c_int32, vp]
+    L.snn_load_text_corpus.argtypes = [vp, C.c_char_p, vp]
+    L.snn_byte_classes.argtypes = [vp, C.c_int64, vp, C.c_int32]
+    L.snn_step.argtypes = [vp, C.c_int32, C.c_int32, C.c_int32]
+    L.snn_run.argtypes = [vp, C.c_int32, vp, C.c_int64, C.c_int32, vp, vp]
+    L.snn_synchronize.argtypes = [vp]
+    L.snn_get_spikes.argtypes = [vp, vp, C.c_int64]
+    L.snn_get_state.argtypes = [vp, C.c_int32, vp, C.c_int64]
+    L.snn_get_counters.argtypes = [vp, C.POINTER(Counters)]
+    L.snn_semantic_eval.argtypes = [vp, C.c_int64, C.POINTER(Semantic), vp, C.c_int64]
+    L.snn_set_dopamine.argtypes = [vp, C.c_float]
+    L.snn_set_e0.argtypes = [vp, C.c_int32]
+    L.snn_save.argtypes = [vp, C.c_char_p, C.c_int32]
+    L.snn_load.argtypes = [vp, C.c_char_p, C.c_int32]
+    L.snn_stream_generate.argtypes = [vp, C.c_int64, C.c_uint64, C.c_double, C.c_double]
+    L.snn_set_profiling.argtypes = [vp, C.c_int32]
+    L.snn_get_profile.argtypes = [vp, C.POINTER(Profile)]
+    L.snn_propagate.argtypes = [vp, vp, C.c_int64, C.c_int32, vp, vp, C.c_int64, C.c_int32, vp]
+    L.snn_propagate_static.argtypes = L.snn_propagate.argtypes
+    L.snn_nccl_unique_id.argtypes = [vp, C.c_int64]
+    L.snn_set_shard.argtypes = [vp, C.c_int32, C.c_int32, vp, C.c_int64]
+    L.snn_shard_plan.argtypes = [C.POINTER(TopologySpec), C.c_int32, C.c_int32, vp, C.c_int32]
+    return L
 
 
 def propagate(post, w, fanout, spikes, acc, frac_bits=24, stream=None, static=False):
@@ -245,8 +258,10 @@ class Network:
 
     def __init__(self, model=MODEL_STAGE2E, preset=PRESET_REF, device=0, e0=False,
                  phase_offset=0, raster_steps=1024, prop_mode=0, prop_rate=0.01, prop_w_max=0.0,
-                 prop_push=0):
-        L = lib()
+                 prop_push=0, refmath=False):
+        """refmath=True runs the network on the core built with the
+        reference's arithmetic (libsnn_b200_refmath.so)."""
+        L = lib(refmath)
         self.L = L
         cfg = Config()
         self._check(L.snn_config_init(C.byref(cfg), model, preset), None)

@@ -226,3 +226,57 @@ def test_bad_checkpoints_are_refused_without_side_effects(tmp_path):
     assert e.value.code == ERR_IO
     assert np.array_equal(bits(b.state("V")), bits(v0))
     assert b.counters()["step"] == 10
+
+
+def native_section_offset(blob, name):
+    """Byte offset of a section's data in a native checkpoint (u32 magic,
+    u32 version, i32 model, u32 blob bytes, blob, u32 count, then per
+    section char[24] name, u64 bytes, data)."""
+    hb = int(np.frombuffer(blob[12:16], np.uint32)[0])
+    off = 16 + hb
+    count = int(np.frombuffer(blob[off: off + 4], np.uint32)[0])
+    off += 4
+    for _ in range(count):
+        nm = blob[off: off + 24].split(b"\0")[0].decode()
+        nb = int(np.frombuffer(blob[off + 24: off + 32], np.uint64)[0])
+        off += 32
+        if nm == name:
+            return off, nb
+        off += nb
+    raise KeyError(name)
+
+
+@pytest.mark.gpu
+def test_microbench_checkpoint_weights_out_of_range_are_refused(tmp_path):
+    """A microbench checkpoint whose excitatory weight lies above w_max (or
+    an inhibitory one above 0) is refused before anything reaches the
+    device: the push's int32 sums and the plasticity clamps rely on the
+    ranges."""
+    def make():
+        n = snn.Network(model=snn.MODEL_PROP, prop_mode=1, prop_rate=0.02)
+        n.build_columns(snn.topology(snn.MODEL_PROP, l4=30000, deg_intra=400))
+        return n
+    good = str(tmp_path / "p.snbn")
+    a = make()
+    a.run(20)
+    a.save(good, snn.FMT_NATIVE)
+    blob = bytearray(open(good, "rb").read())
+    off, nb = native_section_offset(bytes(blob), "w")
+    w = np.frombuffer(bytes(blob[off: off + nb]), np.float32)
+    w_max = float(np.abs(w).max())
+    b = make()
+    b.run(5)
+    v0, w0 = b.state("V").copy(), b.state("weight").copy()
+    for idx, val in ((3, 2.0 * w_max + 1.0), (w.size - 2, 0.5), (7, float("nan"))):
+        bad = bytearray(blob)
+        bad[off + 4 * idx: off + 4 * idx + 4] = np.float32(val).tobytes()
+        p = str(tmp_path / f"bad{idx}.snbn")
+        open(p, "wb").write(bytes(bad))
+        with pytest.raises(snn.SnnError) as e:
+            b.load(p, snn.FMT_NATIVE)
+        assert e.value.code == ERR_IO
+    assert np.array_equal(bits(b.state("V")), bits(v0))
+    assert np.array_equal(bits(b.state("weight")), bits(w0))
+    assert b.counters()["step"] == 5
+    b.load(good, snn.FMT_NATIVE)
+    assert b.counters()["step"] == 20

@@ -54,8 +54,8 @@ def compare_state(net, orc, tag):
 
 
 def run_pair(ncol, steps, corpus_seed=7, phase_offset=0, e0=False, chunk=None, threads=0,
-             check_state_every=None, preset=0):
-    corpus = snn.stream(20000, seed=corpus_seed)
+             check_state_every=None, preset=0, corpus_bytes=20000, p_cjk=0.452):
+    corpus = snn.stream(corpus_bytes, seed=corpus_seed, p_cjk=p_cjk)
     orc = po.Oracle2e(po.ref_params(ncol, e0=int(e0), phase_offset=phase_offset,
                                     n_threads=threads, preset=preset), corpus)
     net = snn.Network(e0=e0, phase_offset=phase_offset,
@@ -166,3 +166,15 @@ def test_parity_full_reference_network_1000_steps():
     steps: rasters bit-identical every step, all state bit-identical at the end."""
     c = run_pair(50, 1000, chunk=250, threads=0, check_state_every=500)
     assert c["n_synapses"] == 10_700_000 and c["n_neurons"] == 55_000
+
+
+@pytest.mark.gpu
+def test_parity_benchmarked_configuration_1000_steps():
+    """The configuration the throughput line is quoted on: the reference
+    network (50 columns), phase table shifted into SYNAPTOGENIC (phase offset
+    5000, plasticity gain 1), the `ref45` stream (seed 42, 1 MiB), 1,000
+    steps: rasters bit-identical every step, all state bit-identical at steps
+    500 and 1,000, counters equal."""
+    c = run_pair(50, 1000, corpus_seed=42, phase_offset=5000, chunk=250, threads=0,
+                 check_state_every=500, corpus_bytes=1 << 20, p_cjk=0.452)
+    assert c["n_synapses"] == 10_700_000 and c["ltp_visits"] > 0

@@ -52,3 +52,25 @@ def test_static_rejects_oversize_input():
     with pytest.raises(snn.SnnError) as e:
         snn.propagate(tp, tw, 1, ts, acc, static=True)
     assert e.value.code == 1 and "static scratch" in str(e.value)
+
+
+@pytest.mark.gpu
+def test_static_calls_allocate_nothing():
+    """After a warm-up call, static calls of several sizes leave the device's
+    free memory exactly as it was (no cudaMalloc behind them)."""
+    import torch
+    dev = torch.device("cuda:0")
+    n_post = 40000
+    bufs = []
+    for n_pre, fanout in ((5000, 64), (200000, 4), (1 << 20, 2)):
+        post, w, sp = arrays(n_pre, fanout, n_post, seed=7 * n_pre + fanout)
+        bufs.append([torch.from_numpy(a).to(dev) for a in (post, w, sp)] + [fanout])
+    acc = torch.zeros(n_post, dtype=torch.int32, device=dev)
+    tp, tw, ts, f = bufs[0]
+    snn.propagate(tp, tw, f, ts, acc, static=True)
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info(dev)[0]
+    for tp, tw, ts, f in bufs * 2:
+        snn.propagate(tp, tw, f, ts, acc, static=True)
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info(dev)[0] == free0
