@@ -57,7 +57,8 @@ constexpr int TD_DIM = 200;
 constexpr uint32_t GV_D_MASK = 0x1f, GV_FF = 1u << 5, GV_EXC = 1u << 6, GV_ARR = 1u << 7,
                    GV_NEXT = 1u << 8, GV_DISP = 1u << 9,
                    GV_EV = 1u << 10;  // arrival, dispatch or a ring read for the next step
-constexpr int NEU_BLOCK = 128;  // k_neurons CTA size; groups carry their pre's index in it
+constexpr int NEU_BLOCK = 128;  // neurons per k_neurons CTA; groups carry their pre's index in it
+constexpr int NEU_THREADS = 256;  // k_neurons CTA size: the first NEU_BLOCK threads own a neuron, all update groups
 #ifndef NEU_GU
 #define NEU_GU 4   // groups per thread in flight in k_neurons
 #endif
@@ -418,17 +419,17 @@ __device__ __forceinline__ void update_group(const Dev& d, const Consts& k, int 
 //                    (decays, FF recovery), :176-194 / :282 (pre trace),
 //                    :334-387 (STP); one thread per group of the CTA's neurons
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(NEU_BLOCK) k_neurons(Dev d, Consts k) {
+__global__ void __launch_bounds__(NEU_THREADS) k_neurons(Dev d, Consts k) {
     __shared__ unsigned s_hist[NEU_BLOCK];
     __shared__ StepIn s_in;
     __shared__ float s_gate[NEU_BLOCK];  // gate of column s_colA + q
     __shared__ int s_colA;
     const Ctrl* c = d.ctrl;
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    const int i0 = blockIdx.x * NEU_BLOCK;
+    const int i1 = min(i0 + NEU_BLOCK, d.N);
+    const int i = i0 + (int)threadIdx.x;
     const int gi = i < d.n_a ? d.a0 + i : d.pf0 + (i - d.n_a);  // global neuron id
-    const int i0 = blockIdx.x * blockDim.x;
-    const int i1 = min(i0 + (int)blockDim.x, d.N);
-    const bool valid = i < d.N;
+    const bool valid = threadIdx.x < NEU_BLOCK && i < d.N;
     // the neuron's state is loaded first: its latency overlaps the step
     // inputs and gates below
     struct NeuIn {
@@ -446,6 +447,18 @@ __global__ void __launch_bounds__(NEU_BLOCK) k_neurons(Dev d, Consts k) {
     // the CTA's group range and the inhibition scalars (written by the
     // previous step's epilogue, not modified in this kernel)
     const int g0 = d.gbeg[i0], g1 = d.gbeg[i1];
+    // the first NEU_GU groups of every thread are loaded now: their latency
+    // overlaps the step inputs, the gates and the neuron update
+    unsigned m0[NEU_GU];
+    float4 st0[NEU_GU];
+    float2 ex0[NEU_GU];
+#pragma unroll
+    for (int u = 0; u < NEU_GU; ++u) {
+        const int gu = g0 + (int)threadIdx.x + u * NEU_THREADS;
+        m0[u] = gu < g1 ? d.gmeta[gu] : 0u;
+        st0[u] = gu < g1 ? d.gstate[gu] : make_float4(0, 0, 0, 0);
+        ex0[u] = gu < g1 ? d.gextra[gu] : make_float2(0, 0);
+    }
     const int inh_active = c->inh_active, kwta_k = c->kwta_k;
     const float gdrive = c->gdrive;
     if (threadIdx.x == 0) {
@@ -588,9 +601,9 @@ __global__ void __launch_bounds__(NEU_BLOCK) k_neurons(Dev d, Consts k) {
             atomicAdd(&d.ctrl->ltp_visits, (unsigned long long)(d.in_ptr[i + 1] - d.in_ptr[i]));
         }
     }
-    s_hist[threadIdx.x] = hist;
+    if (threadIdx.x < NEU_BLOCK) s_hist[threadIdx.x] = hist;
     const unsigned word = __ballot_sync(0xffffffffu, spike != 0);
-    if ((threadIdx.x & 31) == 0 && (i >> 5) < d.words) {
+    if (threadIdx.x < NEU_BLOCK && (threadIdx.x & 31) == 0 && (i >> 5) < d.words) {
         const long long row = (t - c->raster_base) % d.raster_cap;
         d.raster[row * d.words + (i >> 5)] = word;
         if (d.sharded) d.send[i >> 5] = word;
@@ -598,23 +611,29 @@ __global__ void __launch_bounds__(NEU_BLOCK) k_neurons(Dev d, Consts k) {
     __syncthreads();
     // outgoing synapse groups of this CTA's neurons, one thread per group
     unsigned long long arr_cnt = 0, disp_cnt = 0;
-    // NEU_GU groups per iteration: every load of the iteration is issued
-    // before the first group's stores
-    const int stride = NEU_GU * blockDim.x;
-    for (int g = g0 + (int)threadIdx.x; g < g1; g += stride) {
+#pragma unroll
+    for (int u = 0; u < NEU_GU; ++u) {
+        const int gu = g0 + (int)threadIdx.x + u * NEU_THREADS;
+        if (gu < g1) update_group(d, k, gu, m0[u], st0[u], ex0[u], s_hist[gw_lpre(m0[u])], t, arr_cnt, disp_cnt);
+    }
+    // the rest (CTAs with more than NEU_GU * NEU_THREADS groups), NEU_GU per
+    // iteration: every load of the iteration is issued before the first
+    // group's stores
+    const int stride = NEU_GU * NEU_THREADS;
+    for (int g = g0 + stride + (int)threadIdx.x; g < g1; g += stride) {
         unsigned m[NEU_GU];
         float4 st[NEU_GU];
         float2 ex[NEU_GU];
 #pragma unroll
         for (int u = 0; u < NEU_GU; ++u) {
-            const int gu = g + u * (int)blockDim.x;
+            const int gu = g + u * NEU_THREADS;
             m[u] = gu < g1 ? d.gmeta[gu] : 0u;
             st[u] = gu < g1 ? d.gstate[gu] : make_float4(0, 0, 0, 0);
             ex[u] = gu < g1 ? d.gextra[gu] : make_float2(0, 0);
         }
 #pragma unroll
         for (int u = 0; u < NEU_GU; ++u) {
-            const int gu = g + u * (int)blockDim.x;
+            const int gu = g + u * NEU_THREADS;
             if (gu < g1)
                 update_group(d, k, gu, m[u], st[u], ex[u], s_hist[gw_lpre(m[u])], t, arr_cnt, disp_cnt);
         }
@@ -776,7 +795,7 @@ struct PostCtx {
 struct EvIn {
     unsigned gw, fl;
     int p;
-    float ca, ring, act, e1, e2;
+    float ca, ring;
     float2 cold;
     float4 q;
 };
@@ -785,21 +804,15 @@ __device__ __forceinline__ void ev_load(const Dev& d, const PostCtx& pc, int p, 
                                         unsigned fl, float ca, EvIn& x) {
     x.gw = gw; x.fl = fl; x.p = p; x.ca = ca;
     const int dd = fl & GV_D_MASK;
-    const bool plast = pc.post_spk || (fl & (GV_ARR | GV_DISP)) || pc.do10 || pc.do1000;
+    const bool plast = pc.post_spk || (fl & (GV_ARR | GV_DISP)) || pc.do1000;
     x.ring = 0.0f;
     if ((fl & GV_NEXT) && dd >= 2)
         x.ring = d.val[(long long)p * VAL_SLOTS + (int)(((pc.t + 1 - dd) / 3) & (VAL_SLOTS - 1))];
     x.cold = make_float2(0.0f, 0.0f);
     x.q = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    x.act = x.e1 = x.e2 = 0.0f;
     if (plast) {
         x.cold = d.gcold[gw & 0x3fffffffu];  // x_pre before the arrival jump, R after STP
         x.q = d.ev[p];                       // alpha, beta, auto, elig
-        if (pc.do10) {
-            if (gw >> 31) x.act = d.act[p];
-            x.e1 = d.e1[p];
-            x.e2 = d.e2[p];
-        }
     }
 }
 
@@ -810,7 +823,7 @@ __device__ __forceinline__ float ev_compute(const Dev& d, const Consts& k, const
     const bool ff = x.gw & (1u << 30), exc = x.gw >> 31;
     const int dd = fl & GV_D_MASK;
     const bool arr = fl & GV_ARR, disp = fl & GV_DISP;
-    const bool plast = pc.post_spk || arr || disp || pc.do10 || pc.do1000;
+    const bool plast = pc.post_spk || arr || disp || pc.do1000;
     float term_in = x.ring;
     if (!plast) return term_in;
     float4 q = x.q;
@@ -839,25 +852,6 @@ __device__ __forceinline__ float ev_compute(const Dev& d, const Consts& k, const
         if (dd == 1) term_in = val;
         else d.val[(long long)p * VAL_SLOTS + pc.slot_now] = val;
     }
-    if (pc.do10) {
-        if (exc) {
-            float act = x.act, au = q.z;
-            const float ca4 = pm_mul(pm_mul(pm_mul(ca, ca), ca), ca);
-            const float da = pm_fma(pm_mul(k.ck_k1, ca4), pm_sub(1.0f, act),
-                                    -pm_mul(pm_mul(k.ck_k2, act), k.ck_pp1));
-            const float du = pm_fma(pm_mul(pm_mul(k.ck_k3, act), act), pm_sub(1.0f, au),
-                                    -pm_mul(pm_mul(k.ck_k4, au), k.ck_pp1));
-            act = clampf(pm_fma(da, k.ck_dt, act), 0.0f, 1.0f);
-            au = clampf(pm_fma(du, k.ck_dt, au), 0.0f, 1.0f);
-            d.act[p] = act;
-            q.z = au;
-        }
-        const float a1 = pm_fma(x.e1, k.e1_dec, q.w);
-        const float a2 = pm_fma(x.e2, k.e2_dec, a1);
-        d.e1[p] = a1;
-        d.e2[p] = a2;
-        q.w = 0.0f;
-    }
     if (pc.do1000) {
         float a = pm_mul(q.x, k.psw_decay), bb = pm_mul(q.y, k.psw_decay);
         if (a < k.ab_min) a = k.ab_min;
@@ -866,8 +860,20 @@ __device__ __forceinline__ float ev_compute(const Dev& d, const Consts& k, const
         q.x = a;
         q.y = bb;
     }
-    if (pc.post_spk || arr || pc.do10 || pc.do1000) d.ev[p] = q;
+    if (pc.post_spk || arr || pc.do1000) d.ev[p] = q;
     return term_in;
+}
+
+// CaMKII every 10 steps (synapse_kernels.cu:469-515) of an excitatory synapse
+// from this step's Ca
+__device__ __forceinline__ void camkii(const Consts& k, float ca, float& act, float& au) {
+    const float ca4 = pm_mul(pm_mul(pm_mul(ca, ca), ca), ca);
+    const float da = pm_fma(pm_mul(k.ck_k1, ca4), pm_sub(1.0f, act),
+                            -pm_mul(pm_mul(k.ck_k2, act), k.ck_pp1));
+    const float du = pm_fma(pm_mul(pm_mul(k.ck_k3, act), act), pm_sub(1.0f, au),
+                            -pm_mul(pm_mul(k.ck_k4, au), k.ck_pp1));
+    act = clampf(pm_fma(da, k.ck_dt, act), 0.0f, 1.0f);
+    au = clampf(pm_fma(du, k.ck_dt, au), 0.0f, 1.0f);
 }
 
 __device__ __forceinline__ void prefetch_l2(const void* ptr) {
@@ -934,7 +940,7 @@ __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d,
     pc.do10 = (pc.t % 10 == 0) && !pc.e0;
     pc.do1000 = (pc.t % 1000 == 0);
     pc.slot_now = (int)((pc.t / 3) & (VAL_SLOTS - 1));
-    const bool all_events = pc.do10 || pc.do1000;
+    const bool all_events = pc.do1000;
     const int W = gridDim.x * SYN_WARPS;
     const int w = blockIdx.x * SYN_WARPS + warp;
     auto issue = [&](int j, int buf) {  // lane 0 only
@@ -1014,7 +1020,7 @@ __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d,
                     ca = pm_fma(nm, k.ca_gain, ca);
                     const float cmax = ff ? k.ca_max_ff : k.ca_max;
                     if (ca > cmax) ca = cmax;
-                    if (need) sc[p - a0] = ca;  // read back by the event phase
+                    if (need || pc.do10) sc[p - a0] = ca;  // read back by the event / periodic phase
                     d.ca[p] = ca;
                     const float I = pm_mul(pm_mul(nm, pc.one_m_V), k.i_gain);
                     if (fabsf(I) > k.i_min) part_nmda = pm_add(part_nmda, I);
@@ -1065,6 +1071,45 @@ __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d,
         if (lane == 0) {
             d.nmda_cur[j] = part_nmda;
             d.input[j] = part_in;
+        }
+        // periodic phase (t % 10, synapse_kernels.cu:469-543), after this
+        // step's LTP / LTD of every synapse of the row: CaMKII of the
+        // excitatory synapses from this step's Ca, then the eligibility fold
+        // e1 = e1 d1 + elig, e2 = e2 d2 + e1, elig = 0; streamed over the row
+        // two chunks at a time (coalesced), not through the event queue
+        if (pc.do10) {
+            __syncwarp();  // the event phase's record stores are visible to every lane
+            for (int base = b; base < e; base += 64) {
+                float4 q[2];
+                float t1[2], t2[2], av[2];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int p = base + 32 * h + lane;
+                    q[h] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    t1[h] = t2[h] = av[h] = 0.0f;
+                    if (p < e) {
+                        q[h] = d.ev[p];
+                        t1[h] = d.e1[p];
+                        t2[h] = d.e2[p];
+                        if (sg[p - a0] >> 31) av[h] = d.act[p];
+                    }
+                }
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int p = base + 32 * h + lane;
+                    if (p < e) {
+                        if (sg[p - a0] >> 31) {
+                            camkii(k, sc[p - a0], av[h], q[h].z);
+                            d.act[p] = av[h];
+                        }
+                        const float a1 = pm_fma(t1[h], k.e1_dec, q[h].w);
+                        d.e1[p] = a1;
+                        d.e2[p] = pm_fma(t2[h], k.e2_dec, a1);
+                        q[h].w = 0.0f;
+                        d.ev[p] = q[h];
+                    }
+                }
+            }
         }
         // the whole warp is done with this buffer before lane 0 refills it
         __syncwarp();
@@ -1532,7 +1577,7 @@ struct Engine2e : snnb::Engine {
             k_mirror_groups<<<(unsigned)std::max(1ll, (D.GM + 255) / 256), 256, 0, side>>>(D, K);
             SNN_CUDA(cudaEventRecord(ev_join, side));
         }
-        k_neurons<<<nb, NEU_BLOCK, 0, st>>>(D, K);
+        k_neurons<<<nb, NEU_THREADS, 0, st>>>(D, K);
         if (ev) SNN_CUDA(cudaEventRecordWithFlags(ev[e++], st, fl));
         if (world > 1) {
             const snnb::NcclApi& nc = snnb::nccl();
