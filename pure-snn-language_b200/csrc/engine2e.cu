@@ -943,8 +943,8 @@ __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d,
     const bool all_events = pc.do1000;
     const int W = gridDim.x * SYN_WARPS;
     const int w = blockIdx.x * SYN_WARPS + warp;
-    auto issue = [&](int j, int buf) {  // lane 0 only
-        const int a0 = d.in_ptr[j] & ~3, a1 = (d.in_ptr[j + 1] + 3) & ~3;
+    auto issue = [&](int rb, int re, int buf) {  // lane 0 only: the row [rb, re)
+        const int a0 = rb & ~3, a1 = (re + 3) & ~3;
         const unsigned bytes = (unsigned)(a1 - a0) * 4u;
         unsigned* dst = wbase + 2 * cap * buf;
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -956,11 +956,20 @@ __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d,
     };
     unsigned phases = 0u;  // bit s = parity of the next wait on buffer s
     int it = 0;
-    if (lane == 0 && w < d.N) issue(w, 0);
+    // lane 0 loads the row bounds of the post after next one iteration ahead,
+    // so that issuing a staging copy never waits for them
+    int nb_b = 0, nb_e = 0;
+    if (lane == 0 && w < d.N) {
+        issue(d.in_ptr[w], d.in_ptr[w + 1], 0);
+        if (w + W < d.N) { nb_b = d.in_ptr[w + W]; nb_e = d.in_ptr[w + W + 1]; }
+    }
     for (int j = w; j < d.N; j += W, ++it) {
         const int buf = it & 1;
         const int next = j + W;
-        if (lane == 0 && next < d.N) issue(next, buf ^ 1);
+        if (lane == 0 && next < d.N) {
+            issue(nb_b, nb_e, buf ^ 1);
+            if (next + W < d.N) { nb_b = d.in_ptr[next + W]; nb_e = d.in_ptr[next + W + 1]; }
+        }
         // this neuron's row bounds and scalars, issued before the wait so that
         // their latency overlaps the staging copy
         const int b = d.in_ptr[j], e = d.in_ptr[j + 1];

@@ -110,12 +110,39 @@ __device__ __forceinline__ unsigned warp_append(bool flag, unsigned* cnt, int la
     return base + __popc(m & ((1u << lane) - 1u));
 }
 
+// CTA-aggregated append (P_THREADS threads, every one calls it): one
+// atomicAdd per CTA instead of one per warp, so that the counter's address
+// takes a few thousand additions per step rather than tens of thousands.  The
+// order of the entries is irrelevant to their consumers (int32 sums, and
+// per-entry updates of distinct neurons).
+__device__ __forceinline__ unsigned block_append(bool flag, unsigned* cnt, unsigned* s_cnt) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    constexpr int NW = P_THREADS / 32;
+    const unsigned m = __ballot_sync(0xffffffffu, flag);
+    if (lane == 0) s_cnt[warp] = (unsigned)__popc(m);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned tot = 0;
+        for (int w = 0; w < NW; ++w) {
+            const unsigned c = s_cnt[w];
+            s_cnt[w] = tot;
+            tot += c;
+        }
+        s_cnt[NW] = tot ? atomicAdd(cnt, tot) : 0u;
+    }
+    __syncthreads();
+    const unsigned pos = s_cnt[NW] + s_cnt[warp] + (unsigned)__popc(m & ((1u << lane) - 1u));
+    __syncthreads();  // s_cnt is free again
+    return pos;
+}
+
 // forced spike of neuron j at step tn, appended to the pre-spike list of
 // parity tn & 1 with its STP release and the STP state after it; the state
 // and the spike time are committed by step tn's push, so that the exported
-// state always belongs to the last executed step.  All 32 lanes call it.
+// state always belongs to the last executed step.  Every thread of the CTA
+// calls it.
 template <bool STDP, bool STP>
-__device__ __forceinline__ void select_spike(const PDev& D, int tn, int j, int lane) {
+__device__ __forceinline__ void select_spike(const PDev& D, int tn, int j, unsigned* s_cnt) {
     bool ps = false;
     float rel = 1.0f, uu = 0.0f, rr = 0.0f;
     if (j < D.N) {
@@ -127,7 +154,7 @@ __device__ __forceinline__ void select_spike(const PDev& D, int tn, int j, int l
             rel = snn_prop_stp(&uu, &rr, a >= 0 ? tn - a : -1);
         }
     }
-    const unsigned pos = warp_append(ps, &D.ctrl->n_pre[tn & 1], lane);
+    const unsigned pos = block_append(ps, &D.ctrl->n_pre[tn & 1], s_cnt);
     if (ps) {
         const size_t x = (size_t)(tn & 1) * D.N + pos;
         D.pre_list[x] = j;
@@ -152,8 +179,9 @@ __device__ __forceinline__ void commit_spike(const PDev& D, int i, size_t x, int
 
 template <bool STDP, bool STP>
 __global__ void __launch_bounds__(P_THREADS) k4_select0(PDev D) {
+    __shared__ unsigned s_cnt[P_THREADS / 32 + 1];
     const int j = blockIdx.x * P_THREADS + threadIdx.x;
-    select_spike<STDP, STP>(D, D.ctrl->t_base, j, threadIdx.x & 31);
+    select_spike<STDP, STP>(D, D.ctrl->t_base, j, s_cnt);
 }
 
 template <bool STDP, bool STP>
@@ -481,11 +509,12 @@ __global__ void __launch_bounds__(P_THREADS) k4_lif(PDev D, int k) {
     if (threadIdx.x == 0) blk_spikes = 0;
     __syncthreads();
     if (lane == 0 && m) atomicAdd(&blk_spikes, (unsigned)__popc(m));
+    __shared__ unsigned s_cnt[P_THREADS / 32 + 1];
     if (STDP) {
-        const unsigned pos = warp_append(sp, &C->n_post, lane);
+        const unsigned pos = block_append(sp, &C->n_post, s_cnt);
         if (sp) D.post_list[pos] = j;
     }
-    select_spike<STDP, STP>(D, t + 1, j, lane);
+    select_spike<STDP, STP>(D, t + 1, j, s_cnt);
     __syncthreads();
     if (threadIdx.x == 0 && blk_spikes) atomicAdd(&C->post_spikes, (unsigned long long)blk_spikes);
 }
