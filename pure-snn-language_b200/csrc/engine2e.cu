@@ -771,6 +771,9 @@ __device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, unsigned 
 #ifndef SYN_UNROLL
 #define SYN_UNROLL 4   // 32-synapse chunks whose loads a warp issues together
 #endif
+#ifndef SYN_FOLD_U
+#define SYN_FOLD_U 2   // chunks whose loads the periodic phase issues together
+#endif
 #ifndef SYN_MIN_BLOCKS
 #define SYN_MIN_BLOCKS 3
 #endif
@@ -1085,14 +1088,14 @@ __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d,
         // step's LTP / LTD of every synapse of the row: CaMKII of the
         // excitatory synapses from this step's Ca, then the eligibility fold
         // e1 = e1 d1 + elig, e2 = e2 d2 + e1, elig = 0; streamed over the row
-        // two chunks at a time (coalesced), not through the event queue
+        // SYN_FOLD_U chunks at a time (coalesced), not through the event queue
         if (pc.do10) {
             __syncwarp();  // the event phase's record stores are visible to every lane
-            for (int base = b; base < e; base += 64) {
-                float4 q[2];
-                float t1[2], t2[2], av[2];
+            for (int base = b; base < e; base += 32 * SYN_FOLD_U) {
+                float4 q[SYN_FOLD_U];
+                float t1[SYN_FOLD_U], t2[SYN_FOLD_U], av[SYN_FOLD_U];
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
+                for (int h = 0; h < SYN_FOLD_U; ++h) {
                     const int p = base + 32 * h + lane;
                     q[h] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
                     t1[h] = t2[h] = av[h] = 0.0f;
@@ -1104,7 +1107,7 @@ __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d,
                     }
                 }
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
+                for (int h = 0; h < SYN_FOLD_U; ++h) {
                     const int p = base + 32 * h + lane;
                     if (p < e) {
                         if (sg[p - a0] >> 31) {
