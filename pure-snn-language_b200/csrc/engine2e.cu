@@ -777,7 +777,10 @@ __device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, unsigned 
 #ifndef SYN_MIN_BLOCKS
 #define SYN_MIN_BLOCKS 3
 #endif
-constexpr int SYN_THREADS = 256;       // 8 warps per CTA, each an independent pipeline
+#ifndef SYN_THREADS_CFG
+#define SYN_THREADS_CFG 256
+#endif
+constexpr int SYN_THREADS = SYN_THREADS_CFG;  // 8 warps per CTA, each an independent pipeline
 constexpr int SYN_WARPS = SYN_THREADS / 32;
 constexpr unsigned WAIT_LIMIT = 1u << 24;  // bounded spin (~seconds) before flagging an error
 
