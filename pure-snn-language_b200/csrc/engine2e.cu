@@ -771,6 +771,13 @@ __device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, unsigned 
 #ifndef SYN_UNROLL
 #define SYN_UNROLL 4   // 32-synapse chunks whose loads a warp issues together
 #endif
+// SYN_CA_STAGED 1: the warp stages group ids and Ca values of the next row
+// into shared memory; 0: only the group ids, Ca is read from global memory
+// (the row prefetched into L2 with the staging copy), which halves the
+// staging buffers and leaves that shared memory to L1
+#ifndef SYN_CA_STAGED
+#define SYN_CA_STAGED 0
+#endif
 #ifndef SYN_FOLD_U
 #define SYN_FOLD_U 2   // chunks whose loads the periodic phase issues together
 #endif
@@ -926,8 +933,9 @@ __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d,
     const unsigned lt_mask = (1u << lane) - 1u;
     const int cap = d.tile_cap;  // staged elements per stream per buffer
     // per-warp shared memory: [buf0 gid | buf0 ca | buf1 gid | buf1 ca | queue]
-    unsigned* const wbase = reinterpret_cast<unsigned*>(smem_raw) + (size_t)warp * (4 * cap + d.queue_cap);
-    unsigned* const queue = wbase + 4 * cap;  // position | flags << 16
+    constexpr int NSTR = SYN_CA_STAGED ? 2 : 1;  // staged streams
+    unsigned* const wbase = reinterpret_cast<unsigned*>(smem_raw) + (size_t)warp * (2 * NSTR * cap + d.queue_cap);
+    unsigned* const queue = wbase + 2 * NSTR * cap;  // position | flags << 16
     unsigned long long* const bar = bars[warp];
     if (lane == 0) {
         mbar_init(&bar[0], 1);
@@ -952,12 +960,16 @@ __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d,
     auto issue = [&](int rb, int re, int buf) {  // lane 0 only: the row [rb, re)
         const int a0 = rb & ~3, a1 = (re + 3) & ~3;
         const unsigned bytes = (unsigned)(a1 - a0) * 4u;
-        unsigned* dst = wbase + 2 * cap * buf;
+        unsigned* dst = wbase + NSTR * cap * buf;
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        mbar_expect_tx(&bar[buf], 2u * bytes);
+        mbar_expect_tx(&bar[buf], (unsigned)NSTR * bytes);
         if (bytes > 0) {
             bulk_g2s(dst, d.gid + a0, bytes, &bar[buf]);
+#if SYN_CA_STAGED
             bulk_g2s(dst + cap, d.ca + a0, bytes, &bar[buf]);
+#else
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(d.ca + a0), "r"(bytes) : "memory");
+#endif
         }
     };
     unsigned phases = 0u;  // bit s = parity of the next wait on buffer s
@@ -998,8 +1010,13 @@ __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d,
             return;
         }
         const int a0 = b & ~3;
-        const unsigned* sg = wbase + 2 * cap * buf;
+        const unsigned* sg = wbase + NSTR * cap * buf;
+#if SYN_CA_STAGED
         float* sc = reinterpret_cast<float*>(wbase + 2 * cap * buf + cap);
+#define SYN_CA_AT(p) sc[(p) - a0]
+#else
+#define SYN_CA_AT(p) __ldcg(d.ca + (p))
+#endif
         pc.post_spk = hist_j & 1u;
         pc.one_m_V = pm_sub(k.e_rev, V_j);
         const bool all = all_events || pc.post_spk;
@@ -1015,7 +1032,7 @@ __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d,
             for (int h = 0; h < U; ++h) {
                 const int p = base + 32 * h + lane;
                 gw[h] = p < e ? sg[p - a0] : 0u;
-                cav[h] = p < e ? sc[p - a0] : 0.0f;
+                cav[h] = p < e ? SYN_CA_AT(p) : 0.0f;
             }
 #pragma unroll
             for (int h = 0; h < U; ++h) {
@@ -1035,7 +1052,9 @@ __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d,
                     ca = pm_fma(nm, k.ca_gain, ca);
                     const float cmax = ff ? k.ca_max_ff : k.ca_max;
                     if (ca > cmax) ca = cmax;
+#if SYN_CA_STAGED
                     if (need || pc.do10) sc[p - a0] = ca;  // read back by the event / periodic phase
+#endif
                     d.ca[p] = ca;
                     const float I = pm_mul(pm_mul(nm, pc.one_m_V), k.i_gain);
                     if (fabsf(I) > k.i_min) part_nmda = pm_add(part_nmda, I);
@@ -1065,13 +1084,13 @@ __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d,
                 const unsigned ent = queue[qa];
                 offa = (int)(ent & 0xffffu);
                 const int p = b + offa;
-                ev_load(d, pc, p, sg[p - a0], ent >> 16, sc[p - a0], xa);
+                ev_load(d, pc, p, sg[p - a0], ent >> 16, SYN_CA_AT(p), xa);
             }
             if (qb < qn) {
                 const unsigned ent = queue[qb];
                 offb = (int)(ent & 0xffffu);
                 const int p = b + offb;
-                ev_load(d, pc, p, sg[p - a0], ent >> 16, sc[p - a0], xb);
+                ev_load(d, pc, p, sg[p - a0], ent >> 16, SYN_CA_AT(p), xb);
             }
             const float ta = qa < qn ? ev_compute(d, k, pc, xa) : 0.0f;
             const float tb = qb < qn ? ev_compute(d, k, pc, xb) : 0.0f;
@@ -1096,17 +1115,20 @@ __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d,
             __syncwarp();  // the event phase's record stores are visible to every lane
             for (int base = b; base < e; base += 32 * SYN_FOLD_U) {
                 float4 q[SYN_FOLD_U];
-                float t1[SYN_FOLD_U], t2[SYN_FOLD_U], av[SYN_FOLD_U];
+                float t1[SYN_FOLD_U], t2[SYN_FOLD_U], av[SYN_FOLD_U], cv[SYN_FOLD_U];
 #pragma unroll
                 for (int h = 0; h < SYN_FOLD_U; ++h) {
                     const int p = base + 32 * h + lane;
                     q[h] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                    t1[h] = t2[h] = av[h] = 0.0f;
+                    t1[h] = t2[h] = av[h] = cv[h] = 0.0f;
                     if (p < e) {
                         q[h] = d.ev[p];
                         t1[h] = d.e1[p];
                         t2[h] = d.e2[p];
-                        if (sg[p - a0] >> 31) av[h] = d.act[p];
+                        if (sg[p - a0] >> 31) {
+                            av[h] = d.act[p];
+                            cv[h] = SYN_CA_AT(p);
+                        }
                     }
                 }
 #pragma unroll
@@ -1114,7 +1136,7 @@ __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d,
                     const int p = base + 32 * h + lane;
                     if (p < e) {
                         if (sg[p - a0] >> 31) {
-                            camkii(k, sc[p - a0], av[h], q[h].z);
+                            camkii(k, cv[h], av[h], q[h].z);
                             d.act[p] = av[h];
                         }
                         const float a1 = pm_fma(t1[h], k.e1_dec, q[h].w);
@@ -1495,7 +1517,7 @@ struct Engine2e : snnb::Engine {
             SNN_REQUIRE(max_in < 65536, SNN_ERR_ARG, "in-degree above 65535");
             tile_cap = ((max_in + 6) + 3) & ~3;   // aligned range of any neuron's list
             queue_cap = (max_in + 31) & ~31;
-            const size_t smem = (size_t)SYN_WARPS * (4 * (size_t)tile_cap + queue_cap) * sizeof(unsigned);
+            const size_t smem = (size_t)SYN_WARPS * ((SYN_CA_STAGED ? 4 : 2) * (size_t)tile_cap + queue_cap) * sizeof(unsigned);
             SNN_REQUIRE(smem <= 200 * 1024, SNN_ERR_ARG, "in-degree too large for the staging buffers");
             SNN_CUDA(cudaFuncSetAttribute(k_synapses, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           (int)smem));
