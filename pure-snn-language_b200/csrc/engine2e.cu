@@ -778,6 +778,11 @@ __device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, unsigned 
 #ifndef SYN_CA_STAGED
 #define SYN_CA_STAGED 0
 #endif
+// 1: the dense phase computes Ca / NMDA for every lane and keeps the results
+// with predicated stores and selects instead of branching per lane
+#ifndef SYN_BRANCHLIGHT
+#define SYN_BRANCHLIGHT 1
+#endif
 #ifndef SYN_FOLD_U
 #define SYN_FOLD_U 2   // chunks whose loads the periodic phase issues together
 #endif
@@ -845,6 +850,24 @@ __device__ __forceinline__ float ev_compute(const Dev& d, const Consts& k, const
     const float eta = ff ? k.eta_ff : k.eta;
     const float M = pc.e0 ? 1.0f : (exc ? pc.Mexc : pc.Minh);
     const float pf = pc.e0 ? 1.0f : pm_sub(1.0f, pm_mul(0.5f, q.z));
+#ifdef SYN_EV_BRL
+    if (pc.post_spk) {  // LTP from the pre trace (post spiked); selects, not branches
+        const float dw = pm_fma(x.cold.x, k.a_plus, 0.0f);
+        const float nx = pm_fma(pm_mul(pm_mul(pm_mul(eta, dw), pc.gain), M), pf, q.x);
+        q.x = dw > 0.0f ? nx : q.x;
+        const float ex = pm_sub(ca, k.reb_thr);
+        const float ny = pm_fma(pm_mul(pm_mul(pm_mul(eta, ex), k.reb_gain), pc.gain), M, q.y);
+        q.y = ca > k.reb_thr ? ny : q.y;
+        q.w = pm_add(q.w, dw);
+    }
+    {   // LTD at arrival from the post trace, computed for every lane
+        const float dw = pm_mul(-pc.xpost, k.a_minus);
+        const float ny = pm_fma(pm_mul(pm_mul(pm_mul(eta, -dw), pc.gain), M), pf, q.y);
+        q.y = (arr && dw < 0.0f) ? ny : q.y;
+        const float nw = pm_add(q.w, dw);
+        q.w = arr ? nw : q.w;
+    }
+#else
     if (pc.post_spk) {  // LTP from the pre trace (post spiked)
         const float dw = pm_fma(x.cold.x, k.a_plus, 0.0f);
         if (dw > 0.0f) q.x = pm_fma(pm_mul(pm_mul(pm_mul(eta, dw), pc.gain), M), pf, q.x);
@@ -859,6 +882,7 @@ __device__ __forceinline__ float ev_compute(const Dev& d, const Consts& k, const
         if (dw < 0.0f) q.y = pm_fma(pm_mul(pm_mul(pm_mul(eta, -dw), pc.gain), M), pf, q.y);
         q.w = pm_add(q.w, dw);
     }
+#endif
     if (disp) {  // value this dispatch delivers d steps later
         const float wm = pm_div(pm_mul(k.w_max, q.x), pm_add(q.x, q.y));
         const float val = pm_mul(exc ? wm : -wm, x.cold.y);
@@ -887,6 +911,18 @@ __device__ __forceinline__ void camkii(const Consts& k, float ca, float& act, fl
                             -pm_mul(pm_mul(k.ck_k4, au), k.ck_pp1));
     act = clampf(pm_fma(da, k.ck_dt, act), 0.0f, 1.0f);
     au = clampf(pm_fma(du, k.ck_dt, au), 0.0f, 1.0f);
+}
+
+// group-view gather of the dense phase (SYN_GV_EVL: kept in L1 with the
+// evict-last policy, so that the streamed records pass it by)
+__device__ __forceinline__ float2 ld_view(const float2* p) {
+#ifdef SYN_GV_EVL
+    float2 v;
+    asm volatile("ld.global.nc.L1::evict_last.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "l"(p));
+    return v;
+#else
+    return *p;
+#endif
 }
 
 __device__ __forceinline__ void prefetch_l2(const void* ptr) {
@@ -1037,7 +1073,7 @@ __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d,
 #pragma unroll
             for (int h = 0; h < U; ++h) {
                 const int p = base + 32 * h + lane;
-                hv[h] = p < e ? d.gview[gw[h] & 0x3fffffffu] : make_float2(0.0f, 0.0f);
+                hv[h] = p < e ? ld_view(d.gview + (gw[h] & 0x3fffffffu)) : make_float2(0.0f, 0.0f);
             }
 #pragma unroll
             for (int h = 0; h < U; ++h) {
@@ -1045,6 +1081,23 @@ __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d,
                 const bool v = p < e;
                 const unsigned fl = __float_as_uint(hv[h].y);
                 const bool need = v && (all || (fl & GV_EV));
+#if SYN_BRANCHLIGHT
+                {   // excitatory: Ca and NMDA current, computed for every lane
+                    // (an inhibitory group's NMDA conductance is 0) and kept
+                    // by predicated stores / selects
+                    const bool ex = v && (gw[h] >> 31);
+                    const bool ff = gw[h] & (1u << 30);
+                    float ca = pm_mul(cav[h], ff ? k.dec_ca_ff : k.dec_ca);
+                    const float nm = pm_mul(hv[h].x, pc.mgj);
+                    ca = pm_fma(nm, k.ca_gain, ca);
+                    const float cmax = ff ? k.ca_max_ff : k.ca_max;
+                    ca = ca > cmax ? cmax : ca;
+                    if (ex) d.ca[p] = ca;
+                    const float I = pm_mul(pm_mul(nm, pc.one_m_V), k.i_gain);
+                    const float sum = pm_add(part_nmda, I);
+                    part_nmda = (ex && fabsf(I) > k.i_min) ? sum : part_nmda;
+                }
+#else
                 if (v && (gw[h] >> 31)) {  // excitatory: Ca and NMDA current
                     const bool ff = gw[h] & (1u << 30);
                     float ca = pm_mul(cav[h], ff ? k.dec_ca_ff : k.dec_ca);
@@ -1059,6 +1112,7 @@ __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d,
                     const float I = pm_mul(pm_mul(nm, pc.one_m_V), k.i_gain);
                     if (fabsf(I) > k.i_min) part_nmda = pm_add(part_nmda, I);
                 }
+#endif
                 const unsigned m = __ballot_sync(0xffffffffu, need);
                 if (need) queue[qn + __popc(m & lt_mask)] = (unsigned)(p - b) | (fl << 16);
                 qn += __popc(m);
