@@ -778,7 +778,8 @@ __device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, unsigned 
 #ifndef SYN_CA_STAGED
 #define SYN_CA_STAGED 0
 #endif
-// 1: the dense phase computes Ca / NMDA for every lane and keeps the results
+// 1: the dense phase computes Ca / NMDA for every lane, and the event phase
+// LTD (and the LTP updates) for every queued synapse, keeping the results
 // with predicated stores and selects instead of branching per lane
 #ifndef SYN_BRANCHLIGHT
 #define SYN_BRANCHLIGHT 1
@@ -850,7 +851,7 @@ __device__ __forceinline__ float ev_compute(const Dev& d, const Consts& k, const
     const float eta = ff ? k.eta_ff : k.eta;
     const float M = pc.e0 ? 1.0f : (exc ? pc.Mexc : pc.Minh);
     const float pf = pc.e0 ? 1.0f : pm_sub(1.0f, pm_mul(0.5f, q.z));
-#ifdef SYN_EV_BRL
+#if SYN_BRANCHLIGHT
     if (pc.post_spk) {  // LTP from the pre trace (post spiked); selects, not branches
         const float dw = pm_fma(x.cold.x, k.a_plus, 0.0f);
         const float nx = pm_fma(pm_mul(pm_mul(pm_mul(eta, dw), pc.gain), M), pf, q.x);
