@@ -1800,14 +1800,21 @@ struct Engine2e : snnb::Engine {
                                              (size_t)span * D.words * sizeof(unsigned),
                                              cudaMemcpyDeviceToHost, stream));
                 if (counts_out) {
-                    std::vector<unsigned> tmp((size_t)span * D.words);
-                    SNN_CUDA(cudaMemcpyAsync(tmp.data(), raster.p + row0 * D.words,
-                                             tmp.size() * sizeof(unsigned), cudaMemcpyDeviceToHost,
-                                             stream));
+                    // counted from the caller's copy of the rows when there is
+                    // one, else from a copy of our own
+                    std::vector<unsigned> tmp;
+                    const uint32_t* rows = raster_out ? raster_out + (size_t)done * D.words : nullptr;
+                    if (!rows) {
+                        tmp.resize((size_t)span * D.words);
+                        SNN_CUDA(cudaMemcpyAsync(tmp.data(), raster.p + row0 * D.words,
+                                                 tmp.size() * sizeof(unsigned), cudaMemcpyDeviceToHost,
+                                                 stream));
+                        rows = tmp.data();
+                    }
                     SNN_CUDA(cudaStreamSynchronize(stream));
                     for (int r = 0; r < span; ++r) {
                         int cnt = 0;
-                        for (int w = 0; w < D.words; ++w) cnt += __builtin_popcount(tmp[(size_t)r * D.words + w]);
+                        for (int w = 0; w < D.words; ++w) cnt += __builtin_popcount(rows[(size_t)r * D.words + w]);
                         counts_out[done + r] = cnt;
                     }
                 }
