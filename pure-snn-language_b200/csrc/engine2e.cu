@@ -771,19 +771,6 @@ __device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, unsigned 
 #ifndef SYN_UNROLL
 #define SYN_UNROLL 4   // 32-synapse chunks whose loads a warp issues together
 #endif
-// SYN_CA_STAGED 1: the warp stages group ids and Ca values of the next row
-// into shared memory; 0: only the group ids, Ca is read from global memory
-// (the row prefetched into L2 with the staging copy), which halves the
-// staging buffers and leaves that shared memory to L1
-#ifndef SYN_CA_STAGED
-#define SYN_CA_STAGED 0
-#endif
-// 1: the dense phase computes Ca / NMDA for every lane, and the event phase
-// LTD (and the LTP updates) for every queued synapse, keeping the results
-// with predicated stores and selects instead of branching per lane
-#ifndef SYN_BRANCHLIGHT
-#define SYN_BRANCHLIGHT 1
-#endif
 #ifndef SYN_FOLD_U
 #define SYN_FOLD_U 2   // chunks whose loads the periodic phase issues together
 #endif
@@ -851,7 +838,6 @@ __device__ __forceinline__ float ev_compute(const Dev& d, const Consts& k, const
     const float eta = ff ? k.eta_ff : k.eta;
     const float M = pc.e0 ? 1.0f : (exc ? pc.Mexc : pc.Minh);
     const float pf = pc.e0 ? 1.0f : pm_sub(1.0f, pm_mul(0.5f, q.z));
-#if SYN_BRANCHLIGHT
     if (pc.post_spk) {  // LTP from the pre trace (post spiked); selects, not branches
         const float dw = pm_fma(x.cold.x, k.a_plus, 0.0f);
         const float nx = pm_fma(pm_mul(pm_mul(pm_mul(eta, dw), pc.gain), M), pf, q.x);
@@ -868,22 +854,6 @@ __device__ __forceinline__ float ev_compute(const Dev& d, const Consts& k, const
         const float nw = pm_add(q.w, dw);
         q.w = arr ? nw : q.w;
     }
-#else
-    if (pc.post_spk) {  // LTP from the pre trace (post spiked)
-        const float dw = pm_fma(x.cold.x, k.a_plus, 0.0f);
-        if (dw > 0.0f) q.x = pm_fma(pm_mul(pm_mul(pm_mul(eta, dw), pc.gain), M), pf, q.x);
-        if (ca > k.reb_thr) {
-            const float ex = pm_sub(ca, k.reb_thr);
-            q.y = pm_fma(pm_mul(pm_mul(pm_mul(eta, ex), k.reb_gain), pc.gain), M, q.y);
-        }
-        q.w = pm_add(q.w, dw);
-    }
-    if (arr) {  // LTD at arrival from the post trace
-        const float dw = pm_mul(-pc.xpost, k.a_minus);
-        if (dw < 0.0f) q.y = pm_fma(pm_mul(pm_mul(pm_mul(eta, -dw), pc.gain), M), pf, q.y);
-        q.w = pm_add(q.w, dw);
-    }
-#endif
     if (disp) {  // value this dispatch delivers d steps later
         const float wm = pm_div(pm_mul(k.w_max, q.x), pm_add(q.x, q.y));
         const float val = pm_mul(exc ? wm : -wm, x.cold.y);
@@ -912,18 +882,6 @@ __device__ __forceinline__ void camkii(const Consts& k, float ca, float& act, fl
                             -pm_mul(pm_mul(k.ck_k4, au), k.ck_pp1));
     act = clampf(pm_fma(da, k.ck_dt, act), 0.0f, 1.0f);
     au = clampf(pm_fma(du, k.ck_dt, au), 0.0f, 1.0f);
-}
-
-// group-view gather of the dense phase (SYN_GV_EVL: kept in L1 with the
-// evict-last policy, so that the streamed records pass it by)
-__device__ __forceinline__ float2 ld_view(const float2* p) {
-#ifdef SYN_GV_EVL
-    float2 v;
-    asm volatile("ld.global.nc.L1::evict_last.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "l"(p));
-    return v;
-#else
-    return *p;
-#endif
 }
 
 __device__ __forceinline__ void prefetch_l2(const void* ptr) {
@@ -969,10 +927,11 @@ __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d,
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const unsigned lt_mask = (1u << lane) - 1u;
     const int cap = d.tile_cap;  // staged elements per stream per buffer
-    // per-warp shared memory: [buf0 gid | buf0 ca | buf1 gid | buf1 ca | queue]
-    constexpr int NSTR = SYN_CA_STAGED ? 2 : 1;  // staged streams
-    unsigned* const wbase = reinterpret_cast<unsigned*>(smem_raw) + (size_t)warp * (2 * NSTR * cap + d.queue_cap);
-    unsigned* const queue = wbase + 2 * NSTR * cap;  // position | flags << 16
+    // per-warp shared memory: [buf0 gid | buf1 gid | queue]; Ca is read and
+    // written in global memory (its row is prefetched into L2 with the staging
+    // copy), which leaves the rest of the SM's on-chip memory to L1
+    unsigned* const wbase = reinterpret_cast<unsigned*>(smem_raw) + (size_t)warp * (2 * cap + d.queue_cap);
+    unsigned* const queue = wbase + 2 * cap;  // position | flags << 16
     unsigned long long* const bar = bars[warp];
     if (lane == 0) {
         mbar_init(&bar[0], 1);
@@ -997,16 +956,12 @@ __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d,
     auto issue = [&](int rb, int re, int buf) {  // lane 0 only: the row [rb, re)
         const int a0 = rb & ~3, a1 = (re + 3) & ~3;
         const unsigned bytes = (unsigned)(a1 - a0) * 4u;
-        unsigned* dst = wbase + NSTR * cap * buf;
+        unsigned* dst = wbase + cap * buf;
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        mbar_expect_tx(&bar[buf], (unsigned)NSTR * bytes);
+        mbar_expect_tx(&bar[buf], bytes);
         if (bytes > 0) {
             bulk_g2s(dst, d.gid + a0, bytes, &bar[buf]);
-#if SYN_CA_STAGED
-            bulk_g2s(dst + cap, d.ca + a0, bytes, &bar[buf]);
-#else
             asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(d.ca + a0), "r"(bytes) : "memory");
-#endif
         }
     };
     unsigned phases = 0u;  // bit s = parity of the next wait on buffer s
@@ -1047,13 +1002,7 @@ __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d,
             return;
         }
         const int a0 = b & ~3;
-        const unsigned* sg = wbase + NSTR * cap * buf;
-#if SYN_CA_STAGED
-        float* sc = reinterpret_cast<float*>(wbase + 2 * cap * buf + cap);
-#define SYN_CA_AT(p) sc[(p) - a0]
-#else
-#define SYN_CA_AT(p) __ldcg(d.ca + (p))
-#endif
+        const unsigned* sg = wbase + cap * buf;
         pc.post_spk = hist_j & 1u;
         pc.one_m_V = pm_sub(k.e_rev, V_j);
         const bool all = all_events || pc.post_spk;
@@ -1069,12 +1018,12 @@ __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d,
             for (int h = 0; h < U; ++h) {
                 const int p = base + 32 * h + lane;
                 gw[h] = p < e ? sg[p - a0] : 0u;
-                cav[h] = p < e ? SYN_CA_AT(p) : 0.0f;
+                cav[h] = p < e ? __ldcg(d.ca + p) : 0.0f;
             }
 #pragma unroll
             for (int h = 0; h < U; ++h) {
                 const int p = base + 32 * h + lane;
-                hv[h] = p < e ? ld_view(d.gview + (gw[h] & 0x3fffffffu)) : make_float2(0.0f, 0.0f);
+                hv[h] = p < e ? d.gview[gw[h] & 0x3fffffffu] : make_float2(0.0f, 0.0f);
             }
 #pragma unroll
             for (int h = 0; h < U; ++h) {
@@ -1082,7 +1031,6 @@ __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d,
                 const bool v = p < e;
                 const unsigned fl = __float_as_uint(hv[h].y);
                 const bool need = v && (all || (fl & GV_EV));
-#if SYN_BRANCHLIGHT
                 {   // excitatory: Ca and NMDA current, computed for every lane
                     // (an inhibitory group's NMDA conductance is 0) and kept
                     // by predicated stores / selects
@@ -1098,22 +1046,6 @@ __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d,
                     const float sum = pm_add(part_nmda, I);
                     part_nmda = (ex && fabsf(I) > k.i_min) ? sum : part_nmda;
                 }
-#else
-                if (v && (gw[h] >> 31)) {  // excitatory: Ca and NMDA current
-                    const bool ff = gw[h] & (1u << 30);
-                    float ca = pm_mul(cav[h], ff ? k.dec_ca_ff : k.dec_ca);
-                    const float nm = pm_mul(hv[h].x, pc.mgj);
-                    ca = pm_fma(nm, k.ca_gain, ca);
-                    const float cmax = ff ? k.ca_max_ff : k.ca_max;
-                    if (ca > cmax) ca = cmax;
-#if SYN_CA_STAGED
-                    if (need || pc.do10) sc[p - a0] = ca;  // read back by the event / periodic phase
-#endif
-                    d.ca[p] = ca;
-                    const float I = pm_mul(pm_mul(nm, pc.one_m_V), k.i_gain);
-                    if (fabsf(I) > k.i_min) part_nmda = pm_add(part_nmda, I);
-                }
-#endif
                 const unsigned m = __ballot_sync(0xffffffffu, need);
                 if (need) queue[qn + __popc(m & lt_mask)] = (unsigned)(p - b) | (fl << 16);
                 qn += __popc(m);
@@ -1139,13 +1071,13 @@ __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d,
                 const unsigned ent = queue[qa];
                 offa = (int)(ent & 0xffffu);
                 const int p = b + offa;
-                ev_load(d, pc, p, sg[p - a0], ent >> 16, SYN_CA_AT(p), xa);
+                ev_load(d, pc, p, sg[p - a0], ent >> 16, __ldcg(d.ca + p), xa);
             }
             if (qb < qn) {
                 const unsigned ent = queue[qb];
                 offb = (int)(ent & 0xffffu);
                 const int p = b + offb;
-                ev_load(d, pc, p, sg[p - a0], ent >> 16, SYN_CA_AT(p), xb);
+                ev_load(d, pc, p, sg[p - a0], ent >> 16, __ldcg(d.ca + p), xb);
             }
             const float ta = qa < qn ? ev_compute(d, k, pc, xa) : 0.0f;
             const float tb = qb < qn ? ev_compute(d, k, pc, xb) : 0.0f;
@@ -1182,7 +1114,7 @@ __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d,
                         t2[h] = d.e2[p];
                         if (sg[p - a0] >> 31) {
                             av[h] = d.act[p];
-                            cv[h] = SYN_CA_AT(p);
+                            cv[h] = __ldcg(d.ca + p);
                         }
                     }
                 }
@@ -1572,7 +1504,7 @@ struct Engine2e : snnb::Engine {
             SNN_REQUIRE(max_in < 65536, SNN_ERR_ARG, "in-degree above 65535");
             tile_cap = ((max_in + 6) + 3) & ~3;   // aligned range of any neuron's list
             queue_cap = (max_in + 31) & ~31;
-            const size_t smem = (size_t)SYN_WARPS * ((SYN_CA_STAGED ? 4 : 2) * (size_t)tile_cap + queue_cap) * sizeof(unsigned);
+            const size_t smem = (size_t)SYN_WARPS * (2 * (size_t)tile_cap + queue_cap) * sizeof(unsigned);
             SNN_REQUIRE(smem <= 200 * 1024, SNN_ERR_ARG, "in-degree too large for the staging buffers");
             SNN_CUDA(cudaFuncSetAttribute(k_synapses, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           (int)smem));
