@@ -40,6 +40,7 @@
 #include <cstdio>
 #include <limits>
 #include <memory>
+#include <type_traits>
 #include <nccl.h>
 #include "nccl_dl.h"
 #include "ckpt.h"
@@ -768,19 +769,20 @@ __device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, unsigned 
     return ok != 0;
 }
 
-#ifndef SYN_UNROLL
-#define SYN_UNROLL 4   // 32-synapse chunks whose loads a warp issues together
-#endif
 #ifndef SYN_FOLD_U
 #define SYN_FOLD_U 2   // chunks whose loads the periodic phase issues together
 #endif
 #ifndef SYN_MIN_BLOCKS
-#define SYN_MIN_BLOCKS 3
+#define SYN_MIN_BLOCKS 4
 #endif
 #ifndef SYN_THREADS_CFG
-#define SYN_THREADS_CFG 256
+#define SYN_THREADS_CFG 224
 #endif
-constexpr int SYN_THREADS = SYN_THREADS_CFG;  // 8 warps per CTA, each an independent pipeline
+#ifndef SYN_GRAB_RUN
+#define SYN_GRAB_RUN 2   // consecutive posts per unit of a CTA's post list
+#endif
+// 7 warps per CTA (4 CTAs per SM at 72 registers), each an independent pipeline
+constexpr int SYN_THREADS = SYN_THREADS_CFG;
 constexpr int SYN_WARPS = SYN_THREADS / 32;
 constexpr unsigned WAIT_LIMIT = 1u << 24;  // bounded spin (~seconds) before flagging an error
 
@@ -890,11 +892,11 @@ __device__ __forceinline__ void prefetch_l2(const void* ptr) {
 
 // ---------------------------------------------------------------------------
 // k_synapses: persistent; every warp is an independent pipeline over the
-// post-synaptic neurons j = w, w + W, w + 2W, ... (w its global warp index, W
-// the number of warps).  Lane 0 stages the group ids and Ca values of the
-// warp's next neuron into the warp's own shared-memory buffer with
-// cp.async.bulk (mbarrier per buffer, two buffers) while the warp works on
-// the current one.  Per neuron:
+// post-synaptic neurons it takes from its CTA's list (runs of 2 consecutive
+// posts, the CTAs' runs interleaved over the network).  Lane 0 stages the
+// group ids of the warp's next neuron into the warp's own shared-memory
+// buffer with cp.async.bulk (mbarrier per buffer, two buffers), and prefetches
+// its Ca values into L2, while the warp works on the current one.  Per neuron:
 //   dense phase ..... Ca / NMDA (synapse_kernels.cu:45-121) for every incoming
 //                     synapse (four 32-synapse chunks per iteration); synapses
 //                     that also need plasticity, dispatch or ring work go to a
@@ -912,6 +914,9 @@ __device__ __forceinline__ void prefetch_l2(const void* ptr) {
 __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d, Consts k) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     __shared__ __align__(8) unsigned long long bars[SYN_WARPS][2];
+    __shared__ int s_grab;  // next index of this CTA's post list to hand out
+    if (threadIdx.x == 0) s_grab = 0;
+    __syncthreads();
     if (blockIdx.x == 0) {
         if (threadIdx.x == 0) step_epilogue(d, k);
         // zero the count buffers of step t + 1 (the other parity)
@@ -951,8 +956,19 @@ __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d,
     pc.do1000 = (pc.t % 1000 == 0);
     pc.slot_now = (int)((pc.t / 3) & (VAL_SLOTS - 1));
     const bool all_events = pc.do1000;
-    const int W = gridDim.x * SYN_WARPS;
-    const int w = blockIdx.x * SYN_WARPS + warp;
+    // CTA c owns the runs of R consecutive posts that start at R (c + G i)
+    // (G the grid size); its warps take the posts in order from a
+    // shared-memory counter, each warp taking the post after next while it
+    // stages the next one, so that the warps of a CTA work on neighbouring
+    // posts and finish together (a static share of ~15 posts per warp left
+    // a tail of slow warps; global counters cost more than they save)
+    const int G = gridDim.x;
+    constexpr int R = SYN_GRAB_RUN;
+    auto grab = [&]() -> int {  // lane 0 only; increasing, d.N once past the end
+        const int n = atomicAdd(&s_grab, 1);
+        const long long jj = ((long long)blockIdx.x + (long long)(n / R) * G) * R + n % R;
+        return jj < d.N ? (int)jj : d.N;
+    };
     auto issue = [&](int rb, int re, int buf) {  // lane 0 only: the row [rb, re)
         const int a0 = rb & ~3, a1 = (re + 3) & ~3;
         const unsigned bytes = (unsigned)(a1 - a0) * 4u;
@@ -969,16 +985,24 @@ __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d,
     // lane 0 loads the row bounds of the post after next one iteration ahead,
     // so that issuing a staging copy never waits for them
     int nb_b = 0, nb_e = 0;
-    if (lane == 0 && w < d.N) {
-        issue(d.in_ptr[w], d.in_ptr[w + 1], 0);
-        if (w + W < d.N) { nb_b = d.in_ptr[w + W]; nb_e = d.in_ptr[w + W + 1]; }
+    int j = d.N, jn = d.N;  // this warp's current post (all lanes) / next post (lane 0)
+    if (lane == 0) {
+        j = grab();
+        if (j < d.N) {
+            issue(d.in_ptr[j], d.in_ptr[j + 1], 0);
+            jn = grab();
+            if (jn < d.N) { nb_b = d.in_ptr[jn]; nb_e = d.in_ptr[jn + 1]; }
+        }
     }
-    for (int j = w; j < d.N; j += W, ++it) {
+    j = __shfl_sync(0xffffffffu, j, 0);
+    for (; j < d.N; ++it) {
         const int buf = it & 1;
-        const int next = j + W;
-        if (lane == 0 && next < d.N) {
+        const bool has_next = __shfl_sync(0xffffffffu, jn, 0) < d.N;
+        int jnn = d.N;
+        if (lane == 0 && jn < d.N) {
             issue(nb_b, nb_e, buf ^ 1);
-            if (next + W < d.N) { nb_b = d.in_ptr[next + W]; nb_e = d.in_ptr[next + W + 1]; }
+            jnn = grab();
+            if (jnn < d.N) { nb_b = d.in_ptr[jnn]; nb_e = d.in_ptr[jnn + 1]; }
         }
         // this neuron's row bounds and scalars, issued before the wait so that
         // their latency overlaps the staging copy
@@ -995,7 +1019,7 @@ __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d,
         if (__any_sync(0xffffffffu, !ok)) {
             if (lane == 0) {
                 atomicOr(&d.ctrl->error, 1);
-                if (next < d.N)  // drain the copy already issued (bounded) before exiting
+                if (has_next)  // drain the copy already issued (bounded) before exiting
                     for (unsigned spin = 0; spin < WAIT_LIMIT; ++spin)
                         if (mbar_try_wait(&bar[buf ^ 1], (phases >> (buf ^ 1)) & 1u)) break;
             }
@@ -1008,9 +1032,12 @@ __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d,
         const bool all = all_events || pc.post_spk;
         float part_nmda = 0.0f, part_in = 0.0f;
         int qn = 0;
-        // dense phase: four chunks per iteration, all loads issued first
-        constexpr int U = SYN_UNROLL;
-        for (int base = b; base < e; base += 32 * U) {
+        // dense phase: four chunks per iteration, all loads issued first; the
+        // row's last 1-3 chunks go through a body of exactly that many chunks
+        // (rows hold 6.6 chunks on average: padding them to a multiple of four
+        // left a quarter of the dense phase's lanes idle)
+        auto dense = [&](auto u_const, int base) {
+            constexpr int U = decltype(u_const)::value;
             unsigned gw[U];
             float2 hv[U];
             float cav[U];
@@ -1049,6 +1076,17 @@ __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d,
                 const unsigned m = __ballot_sync(0xffffffffu, need);
                 if (need) queue[qn + __popc(m & lt_mask)] = (unsigned)(p - b) | (fl << 16);
                 qn += __popc(m);
+            }
+        };
+        {
+            const int chunks = (e - b + 31) >> 5;
+            int base = b;
+            for (int q = 0; q + 4 <= chunks; q += 4, base += 128) dense(std::integral_constant<int, 4>{}, base);
+            switch (chunks & 3) {
+                case 3: dense(std::integral_constant<int, 3>{}, base); break;
+                case 2: dense(std::integral_constant<int, 2>{}, base); break;
+                case 1: dense(std::integral_constant<int, 1>{}, base); break;
+                default: break;
             }
         }
         __syncwarp();
@@ -1137,6 +1175,8 @@ __global__ void __launch_bounds__(SYN_THREADS, SYN_MIN_BLOCKS) k_synapses(Dev d,
         }
         // the whole warp is done with this buffer before lane 0 refills it
         __syncwarp();
+        j = __shfl_sync(0xffffffffu, jn, 0);
+        jn = jnn;
     }
 }
 
