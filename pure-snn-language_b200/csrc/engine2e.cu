@@ -770,7 +770,7 @@ __device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, unsigned 
 }
 
 #ifndef SYN_FOLD_U
-#define SYN_FOLD_U 2   // chunks whose loads the periodic phase issues together
+#define SYN_FOLD_U 3   // chunks whose loads the periodic phase issues together
 #endif
 #ifndef SYN_MIN_BLOCKS
 #define SYN_MIN_BLOCKS 4
