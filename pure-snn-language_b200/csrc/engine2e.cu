@@ -1248,9 +1248,15 @@ struct Engine2e : snnb::Engine {
     long long steps = 0;
     int raster_cap = 1024;
     long long raster_base_host = 0;  // first step of the current raster rows
-    cudaGraph_t graph = nullptr;
-    cudaGraphExec_t graph_exec = nullptr;
-    int graph_steps = 0;
+    // step graphs by length (kernels read the step from device memory, so a
+    // graph of n steps serves any n consecutive steps), most recently used last
+    struct StepGraph {
+        int n;
+        cudaGraph_t g;
+        cudaGraphExec_t x;
+    };
+    std::vector<StepGraph> graphs;
+    static constexpr size_t kMaxGraphs = 4;
     // profiling: level 1 = events around every kernel of every step; level 2
     // = one event pair around each run call (no event inside the steps)
     bool profiling = false;
@@ -1299,8 +1305,11 @@ struct Engine2e : snnb::Engine {
         for (auto e : run_ev)
             if (e) cudaEventDestroy(e);
         // graphs holding NCCL calls go before the communicator
-        if (graph_exec) cudaGraphExecDestroy(graph_exec);
-        if (graph) cudaGraphDestroy(graph);
+        for (auto& sg : graphs) {
+            cudaGraphExecDestroy(sg.x);
+            cudaGraphDestroy(sg.g);
+        }
+        graphs.clear();
         if (stream) cudaStreamSynchronize(stream);
         if (comm) snnb::nccl().CommDestroy(comm);
         if (side) {
@@ -1615,12 +1624,13 @@ struct Engine2e : snnb::Engine {
         SNN_CUDA(cudaStreamSynchronize(stream));
     }
 
+    // callers synchronize the stream first
     void drop_graph() {
-        if (graph_exec) cudaGraphExecDestroy(graph_exec);
-        if (graph) cudaGraphDestroy(graph);
-        graph_exec = nullptr;
-        graph = nullptr;
-        graph_steps = 0;
+        for (auto& sg : graphs) {
+            cudaGraphExecDestroy(sg.x);
+            cudaGraphDestroy(sg.g);
+        }
+        graphs.clear();
     }
 
     // kernels (timing slots) per step: control, neurons, [exchange + mirror
@@ -1687,16 +1697,32 @@ struct Engine2e : snnb::Engine {
         prof.steps += n;
     }
 
-    // a graph of `n` steps (kernels read the step from device memory)
-    void ensure_graph(int n) {
-        if (graph_exec && graph_steps == n) return;
-        drop_graph();
+    // the graph of `n` steps, captured on first use; the least recently used
+    // of more than kMaxGraphs lengths is released (after the stream drains)
+    cudaGraphExec_t graph_for(int n) {
+        for (size_t i = 0; i < graphs.size(); ++i)
+            if (graphs[i].n == n) {
+                const StepGraph sg = graphs[i];
+                graphs.erase(graphs.begin() + (long)i);
+                graphs.push_back(sg);
+                return sg.x;
+            }
+        if (graphs.size() >= kMaxGraphs) {
+            SNN_CUDA(cudaStreamSynchronize(stream));
+            cudaGraphExecDestroy(graphs.front().x);
+            cudaGraphDestroy(graphs.front().g);
+            graphs.erase(graphs.begin());
+        }
         if (profiling) ensure_events(n);
+        StepGraph sg{n, nullptr, nullptr};
         SNN_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
         for (int q = 0; q < n; ++q) launch_step(stream, profiling ? &pev[(size_t)nslot() * q] : nullptr, true);
-        SNN_CUDA(cudaStreamEndCapture(stream, &graph));
-        SNN_CUDA(cudaGraphInstantiate(&graph_exec, graph, 0));
-        graph_steps = n;
+        SNN_CUDA(cudaStreamEndCapture(stream, &sg.g));
+        const cudaError_t ie = cudaGraphInstantiate(&sg.x, sg.g, 0);
+        if (ie != cudaSuccess) cudaGraphDestroy(sg.g);
+        SNN_CUDA(ie);
+        graphs.push_back(sg);
+        return sg.x;
     }
 
     void set_profiling(int32_t en) override {
@@ -1741,28 +1767,26 @@ struct Engine2e : snnb::Engine {
         }
         int done = 0;
         const int chunk = 50;
-        if (prof_level == 2) {  // graph built before the first event: no host work timed
-            if (n_steps >= chunk) ensure_graph(chunk);
+        // raster rows wrap every raster_cap steps: the run is cut into spans
+        // that end at a wrap, each span into graphs of `chunk` steps and one
+        // of the remainder
+        auto span_at = [&](int d0) { return std::min(n_steps - d0, raster_cap - (d0 % raster_cap)); };
+        if (prof_level == 2) {  // every graph built before the first event: no host work timed
+            for (int d0 = 0; d0 < n_steps; d0 += span_at(d0)) {
+                const int sp = span_at(d0);
+                if (sp >= chunk) graph_for(chunk);
+                if (sp % chunk) graph_for(sp % chunk);
+            }
             SNN_CUDA(cudaEventRecord(run_ev[0], stream));
         }
         while (done < n_steps) {
-            int left = n_steps - done;
-            // raster rows wrap every raster_cap steps: drain before overwriting
-            int span = std::min(left, raster_cap - (done % raster_cap));
+            const int span = span_at(done);  // rows drained before they are overwritten
             int q = 0;
             while (q < span) {
-                if (span - q >= chunk) {
-                    ensure_graph(chunk);
-                    SNN_CUDA(cudaGraphLaunch(graph_exec, stream));
-                    if (profiling) harvest(chunk, steps + done + q);
-                    q += chunk;
-                } else {
-                    if (profiling) ensure_events(1);
-                    launch_step(stream, profiling ? &pev[0] : nullptr);
-                    SNN_CUDA(cudaGetLastError());
-                    if (profiling) harvest(1, steps + done + q);
-                    q += 1;
-                }
+                const int m = std::min(chunk, span - q);
+                SNN_CUDA(cudaGraphLaunch(graph_for(m), stream));
+                if (profiling) harvest(m, steps + done + q);
+                q += m;
             }
             if (raster_out || counts_out) {
                 const long long row0 = (done % raster_cap);
