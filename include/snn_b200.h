@@ -245,7 +245,13 @@ int snn_step(snn_ctx* ctx, int32_t step, int32_t inject_byte, int32_t learn);
 /* n_steps steps as one call, with no host synchronisation between steps.
  * bytes (nullable) replaces the corpus for this and later calls.  If
  * raster_out is non-null it receives n_steps spike bitmasks of
- * ceil(N/32) words each; counts_out (nullable) receives n_steps spike counts. */
+ * ceil(N/32) words each; counts_out (nullable) receives n_steps spike counts.
+ * Stage 2e runs the steps as CUDA graphs on the context's own stream: graphs
+ * of 50 steps and one of the remainder, captured the first time a length is
+ * needed (a few milliseconds) and kept for the four most recently used
+ * lengths, so repeated calls of one size replay graphs.  snn_step is a call of
+ * one step.  Do not call these while the calling thread is capturing a
+ * stream of its own. */
 int snn_run(snn_ctx* ctx, int32_t n_steps, const uint8_t* bytes, int64_t n_bytes,
             int32_t learn, uint32_t* raster_out, int32_t* counts_out);
 
